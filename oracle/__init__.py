@@ -1,0 +1,9 @@
+"""CPU oracle (test infrastructure only): see ``oracle/rel_attn_oracle.py``."""
+from .rel_attn_oracle import (  # noqa: F401
+    rel_attn,
+    rel_attn_rows,
+    round_to_bf16,
+    bf16_bits_to_f32,
+    f32_to_bf16_bits,
+    alignment_offsets,
+)

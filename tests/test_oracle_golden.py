@@ -1,0 +1,75 @@
+"""Pin the CPU oracle (oracle/rel_attn_oracle.py) against the reference's own outputs."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from golden_cases import checksums, load_case, names
+
+
+@pytest.mark.parametrize("name", names())
+def test_inputs_rebuild_bit_identically(name):
+    spec, case, _, stored = load_case(name)
+    np.testing.assert_array_equal(np.array(checksums(case)), stored)
+
+
+@pytest.mark.parametrize("name", names())
+def test_oracle_matches_reference_output(name):
+    spec, c, expected, _ = load_case(name)
+    got = oracle.rel_attn(c.q.float().numpy(), c.k.float().numpy(), c.v.float().numpy(),
+                          c.rel.float().numpy(), c.cu_q.numpy(), c.cu_k.numpy(), spec["scale"],
+                          spec["rel_extent"], causal=spec["causal"],
+                          window_left=spec["window_left"], out_bf16=spec["dtype"] == "bf16")
+    nan_exp = np.isnan(expected)
+    np.testing.assert_array_equal(np.isnan(got), nan_exp)
+    if spec["dtype"] == "bf16":
+        # identical algorithm in fp32: the two results may round to neighbouring bf16 values,
+        # and values near zero (cancellation) carry fp32 summation-order noise of ~1e-6
+        a, b = got[~nan_exp], expected[~nan_exp]
+        tol = np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + 1e-5
+        assert np.all(np.abs(a - b) <= tol), float(np.abs(a - b).max())
+    else:
+        np.testing.assert_allclose(got[~nan_exp], expected[~nan_exp], rtol=2e-5, atol=2e-6)
+
+
+def test_row_blocking_is_exact():
+    spec, c, expected, _ = load_case("long_ctx_h8_2")
+    args = (c.q.float().numpy(), c.k.float().numpy(), c.v.float().numpy(), c.rel.float().numpy(),
+            c.cu_q.numpy(), c.cu_k.numpy(), spec["scale"], spec["rel_extent"])
+    a = oracle.rel_attn(*args, row_block=None)
+    b = oracle.rel_attn(*args, row_block=37)
+    np.testing.assert_allclose(a, b, rtol=1e-6, atol=1e-7)
+
+
+def test_bottom_right_equals_reference_when_square():
+    spec, c, _, _ = load_case("ragged_h4_4")
+    args = (c.q.float().numpy(), c.k.float().numpy(), c.v.float().numpy(), c.rel.float().numpy(),
+            c.cu_q.numpy(), c.cu_k.numpy(), spec["scale"], spec["rel_extent"])
+    np.testing.assert_array_equal(oracle.rel_attn(*args, causal_align="reference"),
+                                  oracle.rel_attn(*args, causal_align="bottom_right"))
+
+
+def test_bottom_right_chunk_equals_full_prefill_rows():
+    """Chunked (cache + chunk) in bottom-right alignment equals the last rows of the full
+    square prefill, which the reference pins directly."""
+    from inkling_fa4.workloads import make_case
+    cache, chunk = 150, 70
+    full = make_case([cache + chunk], [cache + chunk], 4, 2, 64, seed=5)
+    args_full = (full.q.float().numpy(), full.k.float().numpy(), full.v.float().numpy(),
+                 full.rel.float().numpy(), full.cu_q.numpy(), full.cu_k.numpy(), 1 / 128, 64)
+    ref_rows = oracle.rel_attn(*args_full)[cache:]
+    q = full.q.float().numpy()[cache:]
+    rel = full.rel.float().numpy()[cache:]
+    got = oracle.rel_attn(q, args_full[1], args_full[2], rel, np.array([0, chunk]),
+                          np.array([0, cache + chunk]), 1 / 128, 64, causal_align="bottom_right")
+    np.testing.assert_allclose(got, ref_rows, rtol=1e-5, atol=1e-6)
+
+
+def test_reference_decode_is_degenerate():
+    """reference alignment with sq=1: the query sees key 0 only (reference.py:36), so the
+    output equals v[0] of its kv head and no bias applies."""
+    spec, c, expected, _ = load_case("decode_h8_2")
+    v0 = c.v[0].float()  # [Hkv, d]
+    g = 8 // 2
+    want = torch.stack([v0[h // g] for h in range(8)]).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(expected[0], want)
