@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Benchmark of the relative-bias flash-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
+
+Headline (``value``): prefill TFLOP/s on the 32k causal GQA 32/8, d=128, R=128 configuration
+(full causal), aggregated over all ranks.  A "step" is one prefill call over
+one 32768-token sequence with all 32 query heads.  FLOPs are algorithmic:
+4 * head_dim * n_heads * (causally visible query/key pairs), the bias gather and masking
+excluded.  Scaling is weak: every rank owns an independent 32k sequence (work shards by
+sequence / KV-head group with no data-path collective); ``value`` = all ranks' FLOPs / the
+slowest rank's time.
+
+Secondary objects in the same JSON line: the sliding-window variant (window 4096), batched
+decode (GB/s and us/step against HBM), the end-to-end number through the
+public API with host buffers (``e2e``), the CPU baseline (the oracle on host cores, bounded
+sample) and SM clocks sampled during the timed region.
+
+``--impl reference`` times the reference's algorithm on the host CPU (the oracle port; the
+reference itself is a Python/Triton package whose CPU path is the torch oracle ref_rel_attn),
+on bounded samples of the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "inkling-fa4-relative-attention_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "prefill TFLOP/s at 32k GQA 32/8 d128 bf16; decode HBM GB/s & us/step"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SEQ, HQ, HKV, D, R = 32768, 32, 8, 128, 128
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return {k: float(j[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name> (a line
+    'dram_bytes_per_launch_full: <int>'), or None."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch_full:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+def visible_pairs_causal(seq, window=None):
+    if window is None:
+        return seq * (seq + 1) // 2
+    w = window + 1  # keys i-window .. i
+    full = max(0, seq - w)
+    return w * (w + 1) // 2 + full * w if seq >= w else seq * (seq + 1) // 2
+
+
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids):
+        self.uuids = [u.lower() for u in uuids]
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f".clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            uuid = parts[1].lower()
+            if self.uuids and not any(u in uuid or uuid in u for u in self.uuids):
+                continue
+            rows.append(parts)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        smax = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        pw = [float(r[4]) for r in rows if r[4].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
+        loaded = [s for s, p in zip(sm, pw) if p > 300] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------------------------------
+def cpu_baseline_prefill(seconds, window=None, threads=None):
+    """The oracle (torch twin of reference.py's algorithm, all host threads) on a bounded
+    sample of the 32k workload: one head, 128-row blocks spread over the sequence, each row
+    scored densely against all keys as the reference does.  Returns (TFLOP/s, cores, sample)."""
+    import torch
+
+    import oracle
+    from inkling_fa4.workloads import make_case
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    c = make_case([SEQ], [SEQ], 1, 1, R, seed=123, rel_std=0.5)
+    q, k, v, rel = (t[:, 0].float().contiguous() for t in (c.q, c.k, c.v, c.rel))
+    blk = 128
+    order = [((i * 97) % (SEQ // blk)) * blk for i in range(SEQ // blk)]
+    flops, t_used, rows = 0, 0.0, 0
+    for r0 in order:
+        t0 = time.perf_counter()
+        oracle.rel_attn_rows_torch(q[r0:r0 + blk], k, v, rel[r0:r0 + blk],
+                                   torch.arange(r0, r0 + blk), SEQ, SEQ, 1.0 / D, R, True,
+                                   window, "reference")
+        t_used += time.perf_counter() - t0
+        for i in range(r0, r0 + blk):
+            lo = 0 if window is None else max(0, i - window)
+            flops += 4 * D * (i + 1 - lo)
+        rows += blk
+        if t_used >= seconds:
+            break
+    sample = (f"1 of {HQ} heads, {rows} of {SEQ} query rows ({rows // blk} blocks of {blk} "
+              f"spread over the sequence), dense scores against all {SEQ} keys as reference.py "
+              "computes them; algorithmic causal FLOPs")
+    return flops / t_used / 1e12, threads, sample
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    import oracle
+    from inkling_fa4.workloads import make_case
+
+    c = make_case([SEQ], [SEQ], 1, 1, R, seed=123, rel_std=0.5)
+    q, k, v, rel = (t[:, 0].float().contiguous() for t in (c.q, c.k, c.v, c.rel))
+    blk = 64
+    positions = [((i * 97) % (SEQ // blk)) * blk for i in range(SEQ // blk)]
+
+    def step(i):
+        r0 = positions[i % len(positions)]
+        oracle.rel_attn_rows_torch(q[r0:r0 + blk], k, v, rel[r0:r0 + blk],
+                                   torch.arange(r0, r0 + blk), SEQ, SEQ, 1.0 / D, R, True, None,
+                                   "reference")
+        return sum(4 * D * (j + 1) for j in range(r0, r0 + blk))
+
+    for i in range(args.warmup):
+        step(i)
+    flops, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        flops += step(args.warmup + i)
+    dt = time.perf_counter() - t0
+    value = flops / dt / 1e12
+    sample = (f"per step: 1 of {HQ} heads x {blk} query rows of the 32k causal sequence, dense "
+              f"scores against all {SEQ} keys (reference.py's algorithm, oracle port, torch CPU, "
+              f"{threads} threads); algorithmic causal FLOPs")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3 / max(1, args.steps), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "causal32k_gqa32_8_d128_rel128", "seq_len": SEQ,
+                       "n_heads": HQ, "kv_heads": HKV, "head_dim": D, "rel_extent": R},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+def timed(fn, steps, warmup, stream, dist=None, barrier=None):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-window", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                 device_id=torch.device("cuda", local_rank))
+        dist = tdist
+    barrier = (lambda: dist.barrier()) if dist else None
+
+    from inkling_fa4 import (_lib, inkling_fa4_rel_attention_decode_triton,
+                             inkling_fa4_rel_attention_triton)
+    from inkling_fa4.workloads import config_decode, config_long
+
+    peaks, peak_kind = load_peaks()
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(dev)
+
+    # ---------------- headline: 32k causal prefill, inputs resident in HBM
+    c = config_long(device=dev, seed=rank, gen_device=dev)
+    flops = 4 * D * HQ * visible_pairs_causal(SEQ)
+
+    def prefill_step():
+        return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, SEQ, SEQ, R)
+
+    uuids = []
+    try:
+        uuids = [str(torch.cuda.get_device_properties(dev).uuid)]
+    except Exception:
+        pass
+    sampler = ClockSampler(uuids) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = timed(prefill_step, args.steps, args.warmup, stream, dist, barrier)
+    clocks = sampler.stop() if sampler else None
+    ms_step = ms / args.steps
+    value = world * flops * args.steps / (ms / 1e3) / 1e12
+    achieved = flops / (ms_step / 1e3) / 1e12
+    status = _lib.read_device_status(stream.cuda_stream)
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/k/v and N(0,0.5) per-token rel logits, generated on "
+                "the device (rank r uses seed r)",
+        "config": {"workload": "causal32k_gqa32_8_d128_rel128", "batch": 1, "seq_len": SEQ,
+                   "n_heads": HQ, "kv_heads": HKV, "head_dim": D, "rel_extent": R,
+                   "causal": True, "window_left": None, "causal_align": "reference",
+                   "flops_per_step_per_gpu": flops,
+                   "l2": "no flush; inputs of 671 MB per step exceed the 126 MB L2",
+                   "parallelism": f"{world} independent 32k sequences, one per rank (weak)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "peak_source": f"bf16_tflops (burst) of {peak_kind}",
+                     "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
+                     "frac_of_datasheet_2250": achieved / 2250.0,
+                     "traffic": profile_traffic("prefill_causal32k_ncu.txt"),
+                     "kernel": "rel_attn_prefill_kernel (1 launch per step)"},
+        "gpu_launches": args.steps,
+        "device_status": status,
+    }
+    if clocks:
+        result["clocks"] = clocks
+
+    # ---------------- end to end through the public API with host buffers
+    if not args.no_e2e:
+        host = {n: getattr(c, n).cpu().pin_memory() for n in ("q", "k", "v", "rel", "cu_q", "cu_k")}
+        dbuf = {n: torch.empty_like(getattr(c, n)) for n in host}
+        out_host = torch.empty((SEQ, HQ, D), dtype=torch.bfloat16).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        d2h = out_host.numel() * out_host.element_size()
+
+        def e2e_step():
+            for n, t in host.items():
+                dbuf[n].copy_(t, non_blocking=True)
+            o = inkling_fa4_rel_attention_triton(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["rel"],
+                                                 dbuf["cu_q"], dbuf["cu_k"], SEQ, SEQ, R)
+            out_host.copy_(o, non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 10))
+        ems = timed(e2e_step, e_steps, 2, stream, dist, barrier)
+        result["e2e"] = {"value": world * flops * e_steps / (ems / 1e3) / 1e12, "unit": "TFLOP/s",
+                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                         "ms_per_step": ems / e_steps,
+                         "path": "pinned host -> device copies, inkling_fa4_rel_attention_triton "
+                                 "(C ABI), device -> pinned host copy of the output, one stream"}
+        del host, dbuf, out_host
+
+    # ---------------- sliding window 4096 at 32k (BASELINE config 3b)
+    if not args.no_window:
+        wflops = 4 * D * HQ * visible_pairs_causal(SEQ, 4096)
+
+        def win_step():
+            return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, SEQ, SEQ,
+                                                    R, window_size=(4096, 0))
+
+        wms = timed(win_step, args.steps, args.warmup, stream, dist, barrier)
+        result["window32k"] = {"value": world * wflops * args.steps / (wms / 1e3) / 1e12,
+                               "unit": "TFLOP/s", "ms_per_step": wms / args.steps,
+                               "window_left": 4096, "flops_per_step_per_gpu": wflops}
+    del c
+    torch.cuda.empty_cache()
+
+    # ---------------- batched decode
+    if not args.no_decode:
+        dc = config_decode(device=dev, seed=rank, gen_device=dev)
+        lens = dc.seqlens_k
+        kv_bytes = sum(lens) * HKV * D * 2 * 2
+        other = len(lens) * HQ * (D * 2 * 2 + R * 2)
+        dbytes = kv_bytes + other
+        ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+
+        def dec_step():
+            return inkling_fa4_rel_attention_decode_triton(
+                dc.q, dc.k, dc.v, dc.rel, dc.cu_q, dc.cu_k, 1, max(lens), R,
+                causal_align="bottom_right", workspace=ws)
+
+        from inkling_fa4 import _ops
+        p = _ops._decode_params(dc.q, dc.k, dc.v, dc.rel, dc.q, dc.cu_q, dc.cu_k, HQ, HKV, R,
+                                True, -1, "bottom_right", max(lens), 1.0 / D, 0, 0)
+        _, nsplit, chunk = _ops.decode_plan(p)
+        dms = timed(dec_step, args.steps, args.warmup, stream, dist, barrier)
+        us = dms * 1e3 / args.steps
+        gbs = world * dbytes * args.steps / (dms / 1e3) / 1e9
+        per_gpu = dbytes / (us / 1e6) / 1e9
+        result["decode"] = {
+            "value": gbs, "unit": "GB/s", "us_per_step": us,
+            "config": {"workload": "decode128_u1024_32768_gqa32_8_d128_rel128",
+                       "batch": len(lens), "kv_tokens": sum(lens),
+                       "causal_align": "bottom_right", "num_splits": nsplit, "chunk_len": chunk,
+                       "bytes_per_step_per_gpu": dbytes},
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": per_gpu / peaks["hbm_gbs"],
+                         "peak_source": f"hbm_gbs of {peak_kind}",
+                         "traffic": profile_traffic("decode_b128_ncu.txt")},
+            "gpu_launches": args.steps * (2 if nsplit > 1 else 1)}
+        del dc, ws
+        torch.cuda.empty_cache()
+
+    result["device_status"] = _lib.read_device_status(stream.cuda_stream)
+
+    # ---------------- CPU baseline (rank 0, N = 1)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline_prefill(args.cpu_seconds)
+        result["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                  "sample": sample}
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+/*
+ * inkling_fa4 — C ABI of the B200 (sm_100a) relative-position-bias flash attention.
+ *
+ * Plain pointers, integers and floats only.  All tensor pointers are device pointers; the
+ * integer strides are in ELEMENTS.  Every call is asynchronous on the given CUDA stream
+ * (passed as an opaque pointer: a cudaStream_t, or NULL for the legacy default stream) and
+ * performs no host<->device synchronisation, so it can be captured in a CUDA graph.
+ * Every entry point returns 0 on success or a negative IFA4_ERR_* code; the message of the
+ * last failure on the calling thread is available from ifa4_last_error_string().
+ *
+ * Semantics follow the reference oracle ref_rel_attn (src/inkling_fa4/reference.py:4-39 of
+ * KINGXD414/Inkling-FA4-Relative-Attention): scores = (q k^T) * scale; bias
+ * rel[q, h, d] with d = q_pos + bias_shift - k_pos applied only when 0 <= d < rel_extent;
+ * causal mask k_pos <= q_pos + mask_shift; window mask q_pos + mask_shift - k_pos <= window;
+ * GQA kv head = h / (n_heads / kv_heads).  causal_align = IFA4_ALIGN_REFERENCE gives
+ * mask_shift = 0, bias_shift = sq - sk (reference.py:28-37); IFA4_ALIGN_BOTTOM_RIGHT gives
+ * mask_shift = bias_shift = sk - sq.  Rows with no visible key produce 0 (the reference's
+ * Triton kernel behaviour, triton_kernel.py:65-67,79).
+ */
+#ifndef INKLING_FA4_H_
+#define INKLING_FA4_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IFA4_ABI_VERSION 1
+
+enum {
+  IFA4_OK = 0,
+  IFA4_ERR_INVALID_ARGUMENT = -1,  /* null pointer, bad shape/stride/alignment/value   */
+  IFA4_ERR_UNSUPPORTED = -2,       /* valid input the kernels do not implement         */
+  IFA4_ERR_CUDA = -3,              /* a CUDA runtime/driver call failed                 */
+  IFA4_ERR_WORKSPACE = -4,         /* decode workspace missing or too small             */
+  IFA4_ERR_DEVICE_TIMEOUT = -5     /* a kernel gave up on a bounded wait (status word)  */
+};
+
+enum { IFA4_ALIGN_REFERENCE = 0, IFA4_ALIGN_BOTTOM_RIGHT = 1 };
+enum { IFA4_DTYPE_BF16 = 0 };
+
+/* Varlen prefill / chunked prefill / sliding window.
+ * q   [total_q, n_heads, head_dim]     k, v [total_k, kv_heads, head_dim]
+ * rel [total_q, n_heads, >=rel_extent] (rel_stride_t may be 0: a per-head table)
+ * out [total_q, n_heads, head_dim]     cu_seqlens_q/k int32 [batch + 1] on the device.
+ * q/k/v strides and base addresses must be multiples of 16 bytes (TMA); the last dimension
+ * of every tensor is contiguous.  head_dim must be 128. */
+typedef struct IFA4PrefillParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* rel;
+  void* out;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int64_t q_stride_t, q_stride_h;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  int64_t rel_stride_t, rel_stride_h;
+  int64_t out_stride_t, out_stride_h;
+  int64_t total_q;          /* rows of q / rel / out                                  */
+  int64_t total_k;          /* rows of k / v                                          */
+  int32_t batch;
+  int32_t n_heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t rel_extent;
+  int32_t causal;           /* 0 or 1                                                  */
+  int32_t window_left;      /* < 0 disables the sliding window                        */
+  int32_t causal_align;     /* IFA4_ALIGN_*                                            */
+  int32_t max_seqlen_q;     /* grid-size hint; <= 0 means "use total_q". Correctness does
+                               not depend on it (CTAs stride over the query tiles).    */
+  int32_t dtype;            /* IFA4_DTYPE_BF16                                         */
+  float softmax_scale;      /* > 0; the reference uses 1/head_dim                      */
+  int32_t tile_config;      /* 0 = automatic; see ifa4_prefill_tile_config_name        */
+} IFA4PrefillParams;
+
+/* Prefill.  Replaces the per-sequence launch loop of inkling_fa4_rel_attention_triton
+ * (src/inkling_fa4/triton_kernel.py:84-106) and of the KV-pruned variant
+ * (src/inkling_fa4/triton_kernel_kv_pruned.py:210-279): one launch covers all sequences,
+ * cu_seqlens are read on the device, and masked KV tiles are never loaded. */
+int ifa4_prefill_launch(const IFA4PrefillParams* params, void* stream);
+
+/* Single-token decode (one query per sequence: q [batch, n_heads, head_dim], cu_seqlens_q
+ * gives each query's row).  Split-KV: each sequence's visible key range is cut into chunks
+ * of chunk_len keys processed by num_splits CTAs per (sequence, kv head); a combine kernel
+ * merges the fp32 partials. */
+typedef struct IFA4DecodeParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* rel;
+  void* out;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int64_t q_stride_t, q_stride_h;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  int64_t rel_stride_t, rel_stride_h;
+  int64_t out_stride_t, out_stride_h;
+  int64_t total_q;
+  int64_t total_k;
+  int32_t batch;
+  int32_t n_heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t rel_extent;
+  int32_t causal;
+  int32_t window_left;
+  int32_t causal_align;
+  int32_t max_seqlen_k;     /* split-size hint; <= 0 means "use total_k"             */
+  int32_t dtype;
+  float softmax_scale;
+  int32_t num_splits;       /* 0 = automatic (from max_seqlen_k and the SM count)      */
+  int32_t chunk_len;        /* 0 = automatic; otherwise a multiple of 64               */
+} IFA4DecodeParams;
+
+/* Decode.  Replaces inkling_fa4_rel_attention_decode_triton
+ * (src/inkling_fa4/triton_kernel_decode.py:127-170), with the semantics of the oracle
+ * (reference.py:4-39) rather than of that kernel. */
+int ifa4_decode_launch(const IFA4DecodeParams* params, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Bytes of device workspace ifa4_decode_launch needs for these parameters (0 when a single
+ * split suffices).  Resolves num_splits/chunk_len exactly as the launch does; writes them to
+ * *num_splits_out / *chunk_len_out when those are non-null.  No new counterpart in the
+ * reference (its decode has no split-KV); it sizes the caller-owned workspace. */
+int ifa4_decode_workspace_size(const IFA4DecodeParams* params, size_t* bytes_out,
+                               int32_t* num_splits_out, int32_t* chunk_len_out);
+
+/* Reads (and optionally clears) the library's device status word on `stream`, blocking the
+ * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on
+ * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode.  Test hook; the
+ * reference has no counterpart. */
+int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out);
+
+/* Name of the sm_100a prefill tile configuration `tile_config` resolves to (the counterpart
+ * of autotune_configs.get_preset, src/inkling_fa4/autotune_configs.py:61-85). */
+const char* ifa4_prefill_tile_config_name(int32_t tile_config);
+
+/* Message of the last error on the calling thread ("" if none). */
+const char* ifa4_last_error_string(void);
+
+/* IFA4_ABI_VERSION of the loaded library. */
+int32_t ifa4_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INKLING_FA4_H_ */

@@ -1,0 +1,376 @@
+// C ABI of the inkling_fa4 sm_100a kernels: argument validation, TMA descriptor encoding,
+// launch planning, error reporting.  Declared in include/inkling_fa4.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/inkling_fa4.h"
+#include "ifa4_internal.h"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(IFA4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Device status word: kernels OR IFA4 status bits into it when they abandon a bounded wait.
+__device__ int g_ifa4_device_status;
+
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {nullptr};
+int g_sm_count[kMaxDevices] = {0};
+std::mutex g_mu;
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(IFA4_ERR_UNSUPPORTED, "device ordinal %d", *dev);
+  return IFA4_OK;
+}
+
+int device_status_ptr(int** out) {
+  int dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ifa4_device_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  *out = g_status_ptr[dev];
+  return IFA4_OK;
+}
+
+int sm_count(int* out) {
+  int dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    g_sm_count[dev] = n;
+  }
+  *out = g_sm_count[dev];
+  return IFA4_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* fn) {
+  static EncodeTiledFn cached = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q != cudaDriverEntryPointSuccess) err = cudaErrorNotSupported;
+    cached = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (err != cudaSuccess || cached == nullptr)
+    return cuda_fail(err == cudaSuccess ? cudaErrorNotSupported : err,
+                     "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+  *fn = cached;
+  return IFA4_OK;
+}
+
+// [rows, heads, 128] bf16 with element strides (st, sh), boxes of 64 dims x 1 head x box_rows,
+// 128-byte swizzle; out-of-range rows read as zero.
+int encode_rows_heads_dims(CUtensorMap* map, const void* base, int64_t rows, int64_t heads,
+                           int64_t st, int64_t sh, uint32_t box_rows, const char* name) {
+  EncodeTiledFn fn;
+  int rc = get_encode_fn(&fn);
+  if (rc) return rc;
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(sh) * 2, static_cast<cuuint64_t>(st) * 2};
+  cuuint32_t box[3] = {64, 1, box_rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(IFA4_ERR_UNSUPPORTED,
+                "cuTensorMapEncodeTiled(%s) failed with CUresult %d (rows=%lld heads=%lld "
+                "stride_t=%lld stride_h=%lld)",
+                name, static_cast<int>(r), static_cast<long long>(rows),
+                static_cast<long long>(heads), static_cast<long long>(st),
+                static_cast<long long>(sh));
+  return IFA4_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Checks shared by prefill and decode.
+template <class P>
+int validate_common(const P* p, const char* what) {
+  if (p == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: params is NULL", what);
+  if (p->dtype != IFA4_DTYPE_BF16)
+    return fail(IFA4_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16 only)", what, p->dtype);
+  if (p->head_dim != ifa4::kHeadDim)
+    return fail(IFA4_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (128 only)", what, p->head_dim);
+  if (p->batch < 0 || p->total_q < 0 || p->total_k < 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: negative batch/total", what);
+  if (p->n_heads <= 0 || p->kv_heads <= 0 || p->n_heads % p->kv_heads != 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: n_heads %d must be a positive multiple of kv_heads %d",
+                what, p->n_heads, p->kv_heads);
+  if (p->rel_extent <= 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: rel_extent must be > 0", what);
+  if (!(p->softmax_scale > 0.f))
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: softmax_scale must be > 0", what);
+  if (p->causal_align != IFA4_ALIGN_REFERENCE && p->causal_align != IFA4_ALIGN_BOTTOM_RIGHT)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: causal_align %d", what, p->causal_align);
+  if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
+  if (!p->q || !p->k || !p->v || !p->rel || !p->out || !p->cu_seqlens_q || !p->cu_seqlens_k)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: null tensor pointer", what);
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out))
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: q/k/v/out must be 16-byte aligned", what);
+  const int64_t s8[] = {p->q_stride_t, p->q_stride_h, p->k_stride_t, p->k_stride_h,
+                        p->v_stride_t, p->v_stride_h, p->out_stride_t, p->out_stride_h};
+  for (int64_t s : s8)
+    if (s <= 0 || (s % 8) != 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT,
+                  "%s: q/k/v/out token and head strides must be positive multiples of 8 elements",
+                  what);
+  if (p->rel_stride_t < 0 || p->rel_stride_h < 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: negative rel strides", what);
+  if (p->batch > 65535) return fail(IFA4_ERR_UNSUPPORTED, "%s: batch > 65535", what);
+  return IFA4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ifa4_last_error_string(void) { return g_last_error; }
+
+int32_t ifa4_abi_version(void) { return IFA4_ABI_VERSION; }
+
+const char* ifa4_prefill_tile_config_name(int32_t tile_config) {
+  switch (tile_config) {
+    case 0:
+      return "sm100_q2x128_kv128_d128_tmem512_ws12";
+    default:
+      return "";
+  }
+}
+
+int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = validate_common(p, "prefill");
+  if (rc) return rc;
+  if (p->tile_config != 0)
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d unknown", p->tile_config);
+  if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
+  if (p->total_k == 0) {
+    // no keys at all: every row has no visible key -> zeros (handled by the kernel too, but
+    // the K/V tensor maps need at least one row)
+  }
+  int* status = nullptr;
+  if ((rc = device_status_ptr(&status))) return rc;
+
+  ifa4::PrefillKernelArgs a{};
+  a.rel = static_cast<const uint16_t*>(p->rel);
+  a.out = static_cast<uint16_t*>(p->out);
+  a.cu_q = p->cu_seqlens_q;
+  a.cu_k = p->cu_seqlens_k;
+  a.rel_st = p->rel_stride_t;
+  a.rel_sh = p->rel_stride_h;
+  a.out_st = p->out_stride_t;
+  a.out_sh = p->out_stride_h;
+  a.batch = p->batch;
+  a.n_heads = p->n_heads;
+  a.kv_heads = p->kv_heads;
+  a.rel_extent = p->rel_extent;
+  a.causal = p->causal ? 1 : 0;
+  a.window_left = p->window_left < 0 ? -1 : p->window_left;
+  a.align_bottom_right = p->causal_align == IFA4_ALIGN_BOTTOM_RIGHT;
+  const int group = p->n_heads / p->kv_heads;
+  a.pair_heads = (group % 2 == 0) ? 1 : 0;
+  a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  a.status = status;
+
+  CUtensorMap tq, tk, tv;
+  const int64_t krows = p->total_k > 0 ? p->total_k : 1;
+  if ((rc = encode_rows_heads_dims(&tq, p->q, p->total_q, p->n_heads, p->q_stride_t,
+                                   p->q_stride_h, 128, "q")))
+    return rc;
+  if ((rc = encode_rows_heads_dims(&tk, p->k, krows, p->kv_heads, p->k_stride_t, p->k_stride_h,
+                                   128, "k")))
+    return rc;
+  if ((rc = encode_rows_heads_dims(&tv, p->v, krows, p->kv_heads, p->v_stride_t, p->v_stride_h,
+                                   128, "v")))
+    return rc;
+  const int rows_per_cta = a.pair_heads ? 128 : 256;
+  int64_t max_sq = p->max_seqlen_q > 0 ? p->max_seqlen_q : p->total_q;
+  if (max_sq > p->total_q) max_sq = p->total_q;
+  int64_t slots = (max_sq + rows_per_cta - 1) / rows_per_cta;
+  if (slots < 1) slots = 1;
+  if (slots > 65535) slots = 65535;
+  cudaError_t e = ifa4::launch_prefill_sm100(a, tq, tk, tv, static_cast<int>(slots),
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return IFA4_OK;
+}
+
+static int decode_plan(const IFA4DecodeParams* p, int* num_splits, int* chunk_len,
+                       size_t* ws_bytes) {
+  const int group = p->n_heads / p->kv_heads;
+  const int hpc = group < 16 ? group : 16;
+  const int head_blocks = (group + hpc - 1) / hpc;
+  int64_t max_sk = p->max_seqlen_k > 0 ? p->max_seqlen_k : p->total_k;
+  if (max_sk > p->total_k) max_sk = p->total_k;
+  if (max_sk < 1) max_sk = 1;
+  int chunk = p->chunk_len;
+  int splits = p->num_splits;
+  if (chunk < 0 || (chunk % 64) != 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "decode: chunk_len must be a multiple of 64");
+  if (splits < 0) return fail(IFA4_ERR_INVALID_ARGUMENT, "decode: num_splits < 0");
+  if (chunk == 0) {
+    int sms = 148;
+    int rc = sm_count(&sms);
+    if (rc) return rc;
+    const int64_t ctas_per_split = static_cast<int64_t>(p->batch) * p->kv_heads * head_blocks;
+    chunk = 2048;
+    while (chunk > 256 && ctas_per_split * ((max_sk + chunk - 1) / chunk) < 4LL * sms) chunk /= 2;
+  }
+  if (splits == 0) {
+    int64_t s = (max_sk + chunk - 1) / chunk;
+    if (s > 64) s = 64;
+    splits = static_cast<int>(s < 1 ? 1 : s);
+  }
+  if (splits > 65535) return fail(IFA4_ERR_INVALID_ARGUMENT, "decode: num_splits > 65535");
+  *num_splits = splits;
+  *chunk_len = chunk;
+  if (splits == 1) {
+    *ws_bytes = 0;
+  } else {
+    const size_t parts = static_cast<size_t>(p->batch) * p->n_heads * splits;
+    *ws_bytes = parts * 128 * sizeof(float) + parts * sizeof(float);
+  }
+  return IFA4_OK;
+}
+
+int ifa4_decode_workspace_size(const IFA4DecodeParams* p, size_t* bytes_out,
+                               int32_t* num_splits_out, int32_t* chunk_len_out) {
+  g_last_error[0] = '\0';
+  int rc = validate_common(p, "decode");
+  if (rc) return rc;
+  if (bytes_out == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "decode: bytes_out is NULL");
+  int splits = 1, chunk = 64;
+  size_t ws = 0;
+  if (p->batch > 0 && p->total_q > 0) {
+    if ((rc = decode_plan(p, &splits, &chunk, &ws))) return rc;
+  }
+  *bytes_out = ws;
+  if (num_splits_out) *num_splits_out = splits;
+  if (chunk_len_out) *chunk_len_out = chunk;
+  return IFA4_OK;
+}
+
+int ifa4_decode_launch(const IFA4DecodeParams* p, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  g_last_error[0] = '\0';
+  int rc = validate_common(p, "decode");
+  if (rc) return rc;
+  if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
+  if (p->total_q != p->batch)
+    return fail(IFA4_ERR_INVALID_ARGUMENT,
+                "decode: expects exactly one query per sequence (total_q %lld != batch %d)",
+                static_cast<long long>(p->total_q), p->batch);
+  int splits, chunk;
+  size_t ws = 0;
+  if ((rc = decode_plan(p, &splits, &chunk, &ws))) return rc;
+  if (ws > 0 && (workspace == nullptr || workspace_bytes < ws))
+    return fail(IFA4_ERR_WORKSPACE, "decode: workspace of %zu bytes required, got %zu", ws,
+                workspace_bytes);
+  if (ws > 0 && (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+    return fail(IFA4_ERR_WORKSPACE, "decode: workspace must be 16-byte aligned");
+  int* status = nullptr;
+  if ((rc = device_status_ptr(&status))) return rc;
+
+  ifa4::DecodeKernelArgs a{};
+  a.q = static_cast<const uint16_t*>(p->q);
+  a.rel = static_cast<const uint16_t*>(p->rel);
+  a.out = static_cast<uint16_t*>(p->out);
+  a.cu_q = p->cu_seqlens_q;
+  a.cu_k = p->cu_seqlens_k;
+  a.q_st = p->q_stride_t;
+  a.q_sh = p->q_stride_h;
+  a.rel_st = p->rel_stride_t;
+  a.rel_sh = p->rel_stride_h;
+  a.out_st = p->out_stride_t;
+  a.out_sh = p->out_stride_h;
+  a.batch = p->batch;
+  a.n_heads = p->n_heads;
+  a.kv_heads = p->kv_heads;
+  a.rel_extent = p->rel_extent;
+  a.causal = p->causal ? 1 : 0;
+  a.window_left = p->window_left < 0 ? -1 : p->window_left;
+  a.align_bottom_right = p->causal_align == IFA4_ALIGN_BOTTOM_RIGHT;
+  a.group = p->n_heads / p->kv_heads;
+  a.heads_per_cta = a.group < 16 ? a.group : 16;
+  a.num_splits = splits;
+  a.chunk_len = chunk;
+  a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  if (ws > 0) {
+    const size_t parts = static_cast<size_t>(p->batch) * p->n_heads * splits;
+    a.ws_o = static_cast<float*>(workspace);
+    a.ws_lse = a.ws_o + parts * 128;
+  }
+  a.status = status;
+  CUtensorMap tk, tv;
+  const int64_t krows = p->total_k > 0 ? p->total_k : 1;
+  if ((rc = encode_rows_heads_dims(&tk, p->k, krows, p->kv_heads, p->k_stride_t, p->k_stride_h,
+                                   64, "k")))
+    return rc;
+  if ((rc = encode_rows_heads_dims(&tv, p->v, krows, p->kv_heads, p->v_stride_t, p->v_stride_h,
+                                   64, "v")))
+    return rc;
+  cudaError_t e = ifa4::launch_decode_sm100(a, tk, tv, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return IFA4_OK;
+}
+
+int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out) {
+  g_last_error[0] = '\0';
+  if (status_out == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "status_out is NULL");
+  int* dptr = nullptr;
+  int rc = device_status_ptr(&dptr);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, dptr, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (clear && host != 0) {
+    e = cudaMemsetAsync(dptr, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "clear status");
+  }
+  *status_out = host;
+  return IFA4_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,65 @@
+// Internal interface between the C ABI layer (ifa4_capi.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ifa4 {
+
+constexpr int kHeadDim = 128;
+
+// Status bits written by kernels that abandoned a bounded wait.
+constexpr int kStatusPrefillTimeout = 1;
+constexpr int kStatusDecodeTimeout = 2;
+
+struct PrefillKernelArgs {
+  const uint16_t* rel;       // bf16 bits
+  uint16_t* out;             // bf16 bits
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  long long rel_st, rel_sh;
+  long long out_st, out_sh;
+  int batch, n_heads, kv_heads, rel_extent;
+  int causal, window_left, align_bottom_right;
+  int pair_heads;            // 1: the CTA's two sub-tiles are two heads at the same rows
+                             // 0: the CTA's two sub-tiles are consecutive 128-row blocks
+  float scale_log2;          // softmax_scale * log2(e)
+  int* status;
+};
+
+struct PrefillLaunch {
+  dim3 grid;
+  int smem_bytes;
+};
+
+// Builds nothing; launches the tcgen05 prefill kernel.  Returns a cudaError_t.
+cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
+                                 const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                 int q_slots, cudaStream_t stream);
+
+struct DecodeKernelArgs {
+  const uint16_t* q;
+  const uint16_t* rel;
+  uint16_t* out;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  long long q_st, q_sh;
+  long long rel_st, rel_sh;
+  long long out_st, out_sh;
+  int batch, n_heads, kv_heads, rel_extent;
+  int causal, window_left, align_bottom_right;
+  int group;                 // n_heads / kv_heads
+  int heads_per_cta;         // <= 16 query heads of one kv group per CTA
+  int num_splits;            // CTAs per (sequence, head block)
+  int chunk_len;             // keys per chunk (multiple of 64)
+  float scale_log2;
+  float* ws_o;               // [batch, n_heads, num_splits, 128] (num_splits > 1)
+  float* ws_lse;             // [batch, n_heads, num_splits]      (num_splits > 1)
+  int* status;
+};
+
+cudaError_t launch_decode_sm100(const DecodeKernelArgs& args, const CUtensorMap& tm_k,
+                                const CUtensorMap& tm_v, cudaStream_t stream);
+
+}  // namespace ifa4

@@ -1,0 +1,481 @@
+// FA4-style relative-bias flash-attention prefill for sm_100a (B200).
+//
+// One CTA owns two 128-row query sub-tiles that share a KV head ("ping-pong"): either two
+// query heads of one GQA group at the same rows (even group size), or two consecutive 128-row
+// blocks of one head.  Warp roles (12 warps, 384 threads):
+//   warp 0      TMA producer: Q sub-tiles once per work tile, then K/V tiles through a
+//               two-stage ring (128 keys x 128 dims, 128-byte swizzle, no multicast).
+//   warp 1      UMMA issuer (one thread): S_s = Q_s K^T (SS, both K-major) into TMEM, then
+//               O_s += P_s V (TS: P from TMEM, V MN-major) for s = 0, 1, interleaved so the
+//               tensor core works on one sub-tile while the other one's softmax runs.
+//   warp 2      owns the TMEM allocation (512 columns: S0 | S1 | O0 | O1).
+//   warps 4-7   softmax of sub-tile 0, warps 8-11 softmax of sub-tile 1: one thread per
+//               query row (= TMEM lane).  Scale, fused relative-bias gather, causal/window
+//               mask, online softmax in the exp2 domain with conditional O rescaling (only
+//               when the running max grows by more than 2^8), P written back to TMEM as bf16
+//               over the first 64 columns of S, epilogue O / l -> bf16 -> global.
+//
+// Causal and sliding-window masks prune KV tiles before any load: the loop covers exactly the
+// tiles [j_lo, j_hi) that intersect the union of the two sub-tiles' visible key ranges; the
+// per-element mask runs only for rows whose range does not cover the whole tile.
+//
+// Semantics: reference.py:27-39 (oracle) with the kernel-side conventions of
+// triton_kernel.py:43-82 (rows with no visible key give 0, scale applies to QK^T only, the
+// bias is added after scaling).  Bias distance d = q_pos + bias_shift - k_pos with
+// bias_shift = sq - sk (reference alignment) or sk - sq (bottom-right); the mask diagonal is
+// shifted by 0 (reference) or sk - sq (bottom-right).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ifa4_internal.h"
+#include "ifa4_ptx.cuh"
+
+namespace ifa4 {
+namespace prefill {
+
+constexpr int kBM = 128;                                 // query rows per sub-tile
+constexpr int kBN = 128;                                 // keys per KV tile
+constexpr int kThreads = 384;
+constexpr uint32_t kHalf = 128u * 128u;                  // 128 rows x 128 B (64 dims)
+constexpr uint32_t kTile = 2u * kHalf;                   // 128 rows x 256 B (128 dims)
+constexpr uint32_t kSmemQ = 0;                           // 2 sub-tiles
+constexpr uint32_t kSmemK = 2 * kTile;                   // 2 stages
+constexpr uint32_t kSmemV = 4 * kTile;                   // 2 stages
+constexpr uint32_t kSmemBar = 6 * kTile;                 // barriers + slots
+constexpr uint32_t kSmemBytes = kSmemBar + 256;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // slack for 1024-B alignment
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;                // log2 units: rescale O at 256x
+
+constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
+constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
+
+struct Bars {
+  uint64_t q_full, q_empty;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_full[2], o_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+struct TileInfo {
+  int n_kv;      // KV tiles to visit (0: every row of both sub-tiles sees no key)
+  int j_lo;      // first KV tile
+  int head[2];
+  int row0[2];   // first local query row of each sub-tile
+  int kvh;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const PrefillKernelArgs& a, int qt, int hslot,
+                                              int sq, int sk) {
+  TileInfo t;
+  if (a.pair_heads) {
+    t.head[0] = 2 * hslot;
+    t.head[1] = 2 * hslot + 1;
+    t.row0[0] = t.row0[1] = qt * kBM;
+  } else {
+    t.head[0] = t.head[1] = hslot;
+    t.row0[0] = qt * 2 * kBM;
+    t.row0[1] = qt * 2 * kBM + kBM;
+  }
+  t.kvh = t.head[0] / (a.n_heads / a.kv_heads);
+  const int ms = a.align_bottom_right ? sk - sq : 0;
+  int lo = 0x7fffffff, hi = -0x7fffffff;
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const int r0 = t.row0[s];
+    if (r0 >= sq) continue;
+    const int r1 = min(r0 + kBM, sq);
+    int h = sk;
+    if (a.causal) h = min(h, r1 + ms);
+    int l = 0;
+    if (a.window_left >= 0) l = max(0, r0 + ms - a.window_left);
+    if (h > l) {
+      lo = min(lo, l);
+      hi = max(hi, h);
+    }
+  }
+  if (hi <= lo) {
+    t.n_kv = 0;
+    t.j_lo = 0;
+  } else {
+    t.j_lo = lo / kBN;
+    t.n_kv = (hi + kBN - 1) / kBN - t.j_lo;
+  }
+  return t;
+}
+
+__device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+    umma_ss(tmem_s, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
+            kIdescQK, kk > 0 ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_addr,
+                                         bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    umma_ts(tmem_o, tmem_p + kk * 8, sdesc_sw128(v_addr + kk * 2048, kHalf, 1024), kIdescPV,
+            (kk > 0 || accumulate) ? 1u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
+                            const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kSmemBar);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int hslot = blockIdx.x;
+  const int b = blockIdx.y;
+  const int q_start = a.cu_q[b];
+  const int sq = a.cu_q[b + 1] - q_start;
+  const int k_start = a.cu_k[b];
+  const int sk = a.cu_k[b + 1] - k_start;
+  const int rows_per_cta = a.pair_heads ? kBM : 2 * kBM;
+  const int n_qt = (sq + rows_per_cta - 1) / rows_per_cta;
+  if (static_cast<int>(blockIdx.z) >= n_qt) return;  // uniform over the CTA: nothing to do
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], kBM);
+      mbar_init(&bars->o_full[i], 1);
+      mbar_init(&bars->o_empty[i], kBM);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t qc = 0, kc = 0, vc = 0;
+      const uint64_t pol_kv = l2_policy_evict_last();
+      const uint64_t pol_q = l2_policy_evict_first();
+      for (int slot = blockIdx.z; slot < n_qt; slot += gridDim.z) {
+        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+        if (t.n_kv == 0) continue;
+        if (!mbar_wait(&bars->q_empty, (qc & 1) ^ 1, ab)) break;
+        mbar_arrive_expect_tx(&bars->q_full, 2 * kTile);
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d_hint(smem + kSmemQ + s * kTile + hf * kHalf, &tm_q, &bars->q_full,
+                             hf * 64, t.head[s], q_start + t.row0[s], pol_q);
+        ++qc;
+        bool ok = true;
+        for (int j = 0; j < t.n_kv && ok; ++j) {
+          const int row = k_start + (t.j_lo + j) * kBN;
+          const uint32_t ks = kc & 1;
+          if (!(ok = mbar_wait(&bars->k_empty[ks], ((kc >> 1) & 1) ^ 1, ab))) break;
+          mbar_arrive_expect_tx(&bars->k_full[ks], kTile);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d_hint(smem + kSmemK + ks * kTile + hf * kHalf, &tm_k, &bars->k_full[ks],
+                             hf * 64, t.kvh, row, pol_kv);
+          ++kc;
+          const uint32_t vs = vc & 1;
+          if (!(ok = mbar_wait(&bars->v_empty[vs], ((vc >> 1) & 1) ^ 1, ab))) break;
+          mbar_arrive_expect_tx(&bars->v_full[vs], kTile);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d_hint(smem + kSmemV + vs * kTile + hf * kHalf, &tm_v, &bars->v_full[vs],
+                             hf * 64, t.kvh, row, pol_kv);
+          ++vc;
+        }
+        if (!ok) break;
+      }
+      // Drain: every issued load has completed before the CTA may exit (the full barrier of
+      // the last use of each stage has passed that phase once the bytes landed).
+      if (qc > 0) mbar_wait(&bars->q_full, (qc - 1) & 1, ab);
+      for (uint32_t i = 0; i < 2 && i < kc; ++i) {
+        const uint32_t last = kc - 1 - i;
+        mbar_wait(&bars->k_full[last & 1], (last >> 1) & 1, ab);
+      }
+      for (uint32_t i = 0; i < 2 && i < vc; ++i) {
+        const uint32_t last = vc - 1 - i;
+        mbar_wait(&bars->v_full[last & 1], (last >> 1) & 1, ab);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      uint32_t qc = 0, kc = 0, vc = 0, pc = 0, oc = 0;
+      const uint32_t q_addr = smem_u32(smem + kSmemQ);
+      const uint32_t k_addr = smem_u32(smem + kSmemK);
+      const uint32_t v_addr = smem_u32(smem + kSmemV);
+      bool ok = true;
+      for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+        if (t.n_kv == 0) continue;
+        if (!(ok = mbar_wait(&bars->q_full, qc & 1, ab))) break;
+        ++qc;
+        // first KV tile: S_s = Q_s K^T
+        uint32_t ks = kc & 1;
+        if (!(ok = mbar_wait(&bars->k_full[ks], (kc >> 1) & 1, ab))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          issue_qk(tbase + s * 128, q_addr + s * kTile, k_addr + ks * kTile);
+          umma_commit(&bars->s_full[s]);
+        }
+        umma_commit(&bars->k_empty[ks]);
+        ++kc;
+        for (int j = 1; j < t.n_kv && ok; ++j) {
+          ks = kc & 1;
+          const uint32_t vs = vc & 1;
+          if (!(ok = mbar_wait(&bars->k_full[ks], (kc >> 1) & 1, ab))) break;
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            if (!(ok = mbar_wait(&bars->p_full[s], pc & 1, ab))) break;
+            if (j == 1 && !(ok = mbar_wait(&bars->o_empty[s], (oc & 1) ^ 1, ab))) break;
+            if (s == 0 && !(ok = mbar_wait(&bars->v_full[vs], (vc >> 1) & 1, ab))) break;
+            tc_fence_after();
+            issue_pv(tbase + 256 + s * 128, tbase + s * 128, v_addr + vs * kTile, j > 1);
+            issue_qk(tbase + s * 128, q_addr + s * kTile, k_addr + ks * kTile);
+            umma_commit(&bars->s_full[s]);
+          }
+          if (!ok) break;
+          ++pc;
+          umma_commit(&bars->k_empty[ks]);
+          ++kc;
+          umma_commit(&bars->v_empty[vs]);
+          ++vc;
+        }
+        if (!ok) break;
+        // last KV tile: O_s += P_s V
+        const uint32_t vs = vc & 1;
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          if (!(ok = mbar_wait(&bars->p_full[s], pc & 1, ab))) break;
+          if (t.n_kv == 1 && !(ok = mbar_wait(&bars->o_empty[s], (oc & 1) ^ 1, ab))) break;
+          if (s == 0 && !(ok = mbar_wait(&bars->v_full[vs], (vc >> 1) & 1, ab))) break;
+          tc_fence_after();
+          issue_pv(tbase + 256 + s * 128, tbase + s * 128, v_addr + vs * kTile, t.n_kv > 1);
+          umma_commit(&bars->o_full[s]);
+        }
+        if (!ok) break;
+        ++pc;
+        umma_commit(&bars->v_empty[vs]);
+        ++vc;
+        umma_commit(&bars->q_empty);
+        ++oc;
+      }
+      // Drain: all issued MMAs complete before TMEM is released.
+      umma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, ab);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax
+    const int s = (warp - 4) >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tbase + lane_off + s * 128;
+    const uint32_t t_o = tbase + lane_off + 256 + s * 128;
+    const int ms = a.align_bottom_right ? sk - sq : 0;
+    const int bs = a.align_bottom_right ? sk - sq : sq - sk;
+    uint32_t pc = 0, oc = 0;
+    bool ok = true;
+    for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+      const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+      const int qi = t.row0[s] + row;
+      const bool row_valid = qi < sq;
+      const int h = t.head[s];
+      uint16_t* out_row = a.out + static_cast<long long>(q_start + qi) * a.out_st +
+                          static_cast<long long>(h) * a.out_sh;
+      if (t.n_kv == 0) {
+        if (row_valid) {
+          uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) reinterpret_cast<uint4*>(out_row)[c] = z;
+        }
+        continue;
+      }
+      const uint16_t* rel_row = a.rel + static_cast<long long>(q_start + qi) * a.rel_st +
+                                static_cast<long long>(h) * a.rel_sh;
+      // visible keys of this row: [key_lo, key_hi)
+      int key_hi = sk;
+      if (a.causal) key_hi = min(key_hi, qi + ms + 1);
+      const int key_lo = a.window_left >= 0 ? max(0, qi + ms - a.window_left) : 0;
+      const int dmax = qi + bs;  // bias distance at key 0
+      float m_run = -INFINITY, l_run = 0.f;
+
+      for (int j = 0; j < t.n_kv; ++j) {
+        if (!(ok = mbar_wait_warp(&bars->s_full[s], pc & 1, ab))) break;
+        ++pc;
+        tc_fence_after();
+        uint32_t r[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
+        tmem_wait_ld();
+        float x[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[c][i]) * a.scale_log2;
+
+        const int k0 = (t.j_lo + j) * kBN;
+        // relative bias: keys in [dmax - R + 1, dmax] carry rel[row, dmax - key]
+        const int bl = dmax - a.rel_extent + 1 - k0;  // first column with bias
+        const int bh = dmax - k0;                     // last column with bias
+        if (row_valid && bl <= 127 && bh >= 0) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            if (c >= bl && c <= bh) {
+              const uint16_t bits = __ldg(rel_row + (bh - c));
+              x[c] += bf16_bits_to_float(bits) * kLog2e;
+            }
+          }
+        }
+        // mask: only rows whose visible range does not cover the whole tile
+        const int cl = key_lo - k0, ch = key_hi - k0;  // visible columns [cl, ch)
+        if (cl > 0 || ch < kBN) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c < cl || c >= ch) x[c] = -INFINITY;
+        }
+        float m_tile = x[0];
+#pragma unroll
+        for (int c = 1; c < 128; ++c) m_tile = fmaxf(m_tile, x[c]);
+        const float m_new = fmaxf(m_run, m_tile);
+        float alpha = 1.f;
+        bool need_rescale = false;
+        if (j == 0) {
+          m_run = m_new;
+        } else if (m_new > m_run + kRescaleThreshold) {
+          alpha = fast_exp2(m_run - m_new);
+          need_rescale = true;
+          l_run *= alpha;
+          m_run = m_new;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        float lsum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = fast_exp2(x[c * 32 + 2 * i] - m_use);
+            const float p1 = fast_exp2(x[c * 32 + 2 * i + 1] - m_use);
+            lsum += p0 + p1;
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(t_s + c * 16, pk);
+        }
+        l_run += lsum;
+        // Conditional O correction (PV of the previous tile is complete: its commit
+        // preceded this tile's S commit).
+        if (__any_sync(0xffffffffu, need_rescale)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_o + c * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[s]);
+      }
+      if (!ok) break;
+      // epilogue
+      if (!(ok = mbar_wait_warp(&bars->o_full[s], oc & 1, ab))) break;
+      ++oc;
+      tc_fence_after();
+      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(t_o + c * 32, o);
+        tmem_wait_ld();
+        if (row_valid) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
+                                __uint_as_float(o[2 * i + 1]) * inv_l);
+          uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->o_empty[s]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+}  // namespace prefill
+
+cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
+                                 const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                 int q_slots, cudaStream_t stream) {
+  // The dynamic shared-memory limit is a per-device function attribute.
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return de;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(prefill::kSmemAlloc));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int head_slots = args.pair_heads ? args.n_heads / 2 : args.n_heads;
+  dim3 grid(head_slots, args.batch, q_slots);
+  prefill::rel_attn_prefill_kernel<<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(
+      args, tm_q, tm_k, tm_v);
+  return cudaGetLastError();
+}
+
+}  // namespace ifa4

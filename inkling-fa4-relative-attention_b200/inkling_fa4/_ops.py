@@ -1,0 +1,173 @@
+"""Host side of the drop-in API: argument checks mirroring the reference call surface, stride
+handling, and the calls through the C ABI (``_lib``).  Launches go on torch's current CUDA
+stream of the input's device; nothing here synchronises with the device, so the calls can be
+captured in a CUDA graph."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+HEAD_DIM = 128
+ALIGN = {"reference": _lib.IFA4_ALIGN_REFERENCE, "bottom_right": _lib.IFA4_ALIGN_BOTTOM_RIGHT}
+
+
+def _tma_ready(t: torch.Tensor) -> torch.Tensor:
+    """q/k/v go through TMA: last stride 1, other strides multiples of 8 elements (16 bytes),
+    16-byte aligned base.  Anything else is copied to a contiguous tensor."""
+    ok = (t.stride(-1) == 1 and all(s > 0 and s % 8 == 0 for s in t.stride()[:-1])
+          and t.data_ptr() % 16 == 0)
+    return t if ok else t.contiguous()
+
+
+def _check_inputs(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, n_heads, kv_heads,
+                  head_dim, window_size, causal_align):
+    for nm, t in (("q", q), ("k", k), ("v", v), ("rel_logits", rel_logits),
+                  ("cu_seqlens_q", cu_q), ("cu_seqlens_k", cu_k)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name}: {nm} must be a torch.Tensor")
+        if not t.is_cuda:
+            raise ValueError(f"{name}: {nm} must be a CUDA tensor (no CPU path exists)")
+        if t.device != q.device:
+            raise ValueError(f"{name}: {nm} is on {t.device}, q on {q.device}")
+    for nm, t in (("q", q), ("k", k), ("v", v), ("rel_logits", rel_logits)):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name}: {nm} must be bfloat16, got {t.dtype}")
+        if t.dim() != 3:
+            raise ValueError(f"{name}: {nm} must be 3-D")
+    for nm, t in (("cu_seqlens_q", cu_q), ("cu_seqlens_k", cu_k)):
+        if t.dtype != torch.int32 or t.dim() != 1 or t.numel() < 1:
+            raise ValueError(f"{name}: {nm} must be a non-empty 1-D int32 tensor")
+    if cu_q.numel() != cu_k.numel():
+        raise ValueError(f"{name}: cu_seqlens_q and cu_seqlens_k differ in length")
+    if n_heads is None:
+        n_heads = q.shape[1]
+    if kv_heads is None:
+        kv_heads = k.shape[1]
+    if n_heads != q.shape[1] or kv_heads != k.shape[1] or v.shape[1] != kv_heads:
+        raise ValueError(f"{name}: head counts disagree with tensor shapes")
+    if n_heads % kv_heads != 0:
+        raise ValueError(f"{name}: n_heads {n_heads} not a multiple of kv_heads {kv_heads}")
+    if head_dim != HEAD_DIM or q.shape[2] != HEAD_DIM or k.shape[2] != HEAD_DIM or v.shape[2] != HEAD_DIM:
+        raise ValueError(f"{name}: head_dim must be {HEAD_DIM}")
+    if k.shape[0] != v.shape[0]:
+        raise ValueError(f"{name}: k and v differ in token count")
+    if rel_logits.shape[0] != q.shape[0] or rel_logits.shape[1] != n_heads:
+        raise ValueError(f"{name}: rel_logits must be [total_q, n_heads, >=rel_extent]")
+    rel_extent = int(rel_extent)
+    if rel_extent <= 0 or rel_logits.shape[2] < rel_extent:
+        raise ValueError(f"{name}: rel_extent {rel_extent} out of range for rel_logits {tuple(rel_logits.shape)}")
+    if causal_align not in ALIGN:
+        raise ValueError(f"{name}: causal_align must be one of {sorted(ALIGN)}")
+    window_left = int(window_size[0]) if window_size is not None else -1
+    return n_heads, kv_heads, rel_extent, window_left
+
+
+def _fill_common(p, q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
+                 window_left, causal_align):
+    p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    p.rel, p.out = rel.data_ptr(), out.data_ptr()
+    p.cu_seqlens_q, p.cu_seqlens_k = cu_q.data_ptr(), cu_k.data_ptr()
+    p.q_stride_t, p.q_stride_h = q.stride(0), q.stride(1)
+    p.k_stride_t, p.k_stride_h = k.stride(0), k.stride(1)
+    p.v_stride_t, p.v_stride_h = v.stride(0), v.stride(1)
+    p.rel_stride_t, p.rel_stride_h = rel.stride(0), rel.stride(1)
+    p.out_stride_t, p.out_stride_h = out.stride(0), out.stride(1)
+    p.total_q, p.total_k = q.shape[0], k.shape[0]
+    p.batch = cu_q.numel() - 1
+    p.n_heads, p.kv_heads, p.head_dim = n_heads, kv_heads, HEAD_DIM
+    p.rel_extent = rel_extent
+    p.causal = 1 if causal else 0
+    p.window_left = window_left
+    p.causal_align = ALIGN[causal_align]
+    p.dtype = _lib.IFA4_DTYPE_BF16
+
+
+def _prepare(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, causal, window_size, n_heads,
+             kv_heads, head_dim, softmax_scale, causal_align, out):
+    n_heads, kv_heads, rel_extent, window_left = _check_inputs(
+        name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, n_heads, kv_heads, head_dim,
+        window_size, causal_align)
+    q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
+    rel = rel_logits if rel_logits.stride(-1) == 1 else rel_logits.contiguous()
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    else:
+        if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device:
+            raise ValueError(f"{name}: out must match q in shape, dtype and device")
+        if out.stride(-1) != 1 or any(s % 8 for s in out.stride()[:-1]) or out.data_ptr() % 16:
+            raise ValueError(f"{name}: out needs unit last stride, strides multiple of 8, 16-B alignment")
+    scale = (1.0 / HEAD_DIM) if softmax_scale is None else float(softmax_scale)
+    if not scale > 0:
+        raise ValueError(f"{name}: softmax_scale must be > 0")
+    return q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale
+
+
+@torch.no_grad()
+def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+            rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
+            head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
+            tile_config=0):
+    q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
+        "prefill", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
+        window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out)
+    p = _lib.PrefillParams()
+    _fill_common(p, q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
+                 rel_extent, causal, window_left, causal_align)
+    p.max_seqlen_q = int(max_seqlen_q) if max_seqlen_q else 0
+    p.softmax_scale = scale
+    p.tile_config = int(tile_config)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        _lib.check(_lib.lib().ifa4_prefill_launch(ctypes.byref(p), ctypes.c_void_p(stream)))
+    return out
+
+
+def _decode_params(q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
+                   window_left, causal_align, max_seqlen_k, scale, num_splits, chunk_len):
+    p = _lib.DecodeParams()
+    _fill_common(p, q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
+                 window_left, causal_align)
+    p.max_seqlen_k = int(max_seqlen_k) if max_seqlen_k else 0
+    p.softmax_scale = scale
+    p.num_splits = int(num_splits)
+    p.chunk_len = int(chunk_len)
+    return p
+
+
+def decode_plan(p) -> tuple[int, int, int]:
+    """(workspace bytes, num_splits, chunk_len) the library resolves for these parameters."""
+    nbytes = ctypes.c_size_t(0)
+    ns, cl = ctypes.c_int32(0), ctypes.c_int32(0)
+    _lib.check(_lib.lib().ifa4_decode_workspace_size(ctypes.byref(p), ctypes.byref(nbytes),
+                                                     ctypes.byref(ns), ctypes.byref(cl)))
+    return int(nbytes.value), int(ns.value), int(cl.value)
+
+
+@torch.no_grad()
+def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+           rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
+           head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
+           num_splits=0, chunk_len=0, workspace=None):
+    q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
+        "decode", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
+        window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out)
+    if q.shape[0] != cu_seqlens_q.numel() - 1:
+        raise ValueError("decode: expects exactly one query token per sequence")
+    if q.stride(0) % 2 or q.stride(1) % 2:
+        q = q.contiguous()
+    p = _decode_params(q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
+                       rel_extent, causal, window_left, causal_align, max_seqlen_k, scale,
+                       num_splits, chunk_len)
+    with torch.cuda.device(q.device):
+        nbytes, _, _ = decode_plan(p)
+        if nbytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < nbytes):
+            workspace = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        ws_ptr = workspace.data_ptr() if nbytes > 0 else 0
+        ws_len = workspace.numel() * workspace.element_size() if nbytes > 0 else 0
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        _lib.check(_lib.lib().ifa4_decode_launch(ctypes.byref(p), ctypes.c_void_p(ws_ptr),
+                                                 ctypes.c_size_t(ws_len), ctypes.c_void_p(stream)))
+    return out

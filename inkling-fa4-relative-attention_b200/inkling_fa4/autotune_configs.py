@@ -1,0 +1,50 @@
+"""Tile-configuration table (drop-in for src/inkling_fa4/autotune_configs.py).
+
+The reference maps (seq_len, arch) to Triton launch parameters (autotune_configs.py:17-85).
+Here only sm_100a kernels exist, so every architecture key resolves to the sm100 table, whose
+entries describe the hand-written kernels:
+
+* prefill: two 128-row query sub-tiles per CTA (BLOCK_Q = 128 each) against 128-key KV tiles,
+  12 warps (TMA, MMA, TMEM owner, spare, two softmax warpgroups), a 2-stage K and a 2-stage V
+  ring; ``tile_config`` is the id passed through the C ABI.
+* decode: 64-key tiles through a 3-stage TMA ring, 4 consumer warps + 1 producer warp, chunk
+  length and split count chosen by the library from max_seqlen_k and the SM count
+  (``ifa4_decode_workspace_size`` reports them).
+"""
+from __future__ import annotations
+
+import torch
+
+# (max_seq_len, BLOCK_Q, BLOCK_K, num_warps, num_stages, tile_config)
+PRESETS = {
+    "sm100": {
+        "default": (128, 128, 12, 2, 0),
+        "buckets": [],
+    },
+}
+DECODE_PRESET = {"BLOCK_K": 64, "num_warps": 5, "num_stages": 3, "chunk_len": 0, "num_splits": 0}
+
+
+def _detect_arch() -> str:
+    """Compute-capability key of the current GPU, e.g. 'sm100' (reference :53-58)."""
+    if not torch.cuda.is_available():
+        return "sm100"
+    cap = torch.cuda.get_device_capability()
+    return f"sm{cap[0]}{cap[1]}"
+
+
+def get_preset(seq_len: int, arch: str | None = None) -> dict:
+    """Tile configuration for a query length (reference :61-85).  Every arch resolves to sm100."""
+    table = PRESETS["sm100"]
+    entry = table["default"]
+    for bucket in table["buckets"]:
+        if seq_len <= bucket[0]:
+            entry = bucket[1:]
+            break
+    bq, bk, nw, ns, tc = entry
+    if seq_len == 1:
+        return dict(DECODE_PRESET, BLOCK_Q=1)
+    return {"BLOCK_Q": bq, "BLOCK_K": bk, "num_warps": nw, "num_stages": ns, "tile_config": tc}
+
+
+get_config = get_preset  # name used in the reference module docstring

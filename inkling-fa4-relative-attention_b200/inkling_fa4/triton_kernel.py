@@ -1,0 +1,41 @@
+"""Prefill / varlen / chunked / sliding-window entry point (drop-in name).
+
+The module keeps the reference's name (src/inkling_fa4/triton_kernel.py) so existing imports
+keep working; it contains no Triton.  The call goes through the C ABI to the sm_100a
+tcgen05/TMA kernel in csrc/ifa4_prefill_sm100.cu.
+"""
+from __future__ import annotations
+
+from . import _ops
+
+
+def inkling_fa4_rel_attention_triton(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k,
+                                     max_seqlen_q, max_seqlen_k, rel_extent,
+                                     causal=True, window_size=(-1, -1),
+                                     n_heads=None, kv_heads=None, head_dim=128,
+                                     arch=None, *, softmax_scale=None,
+                                     causal_align="reference", out=None):
+    """Relative-position-bias flash attention over packed variable-length sequences.
+
+    Same arguments and meaning as the reference (triton_kernel.py:84-106):
+    q [total_q, n_heads, 128], k/v [total_k, kv_heads, 128], rel_logits
+    [total_q, n_heads, >=rel_extent] (bf16; token stride 0 allowed), cu_seqlens_q/k int32
+    [batch+1] on the device.  ``window_size[0]`` is the left window (-1: none);
+    ``window_size[1]`` is ignored, as in the reference.  ``max_seqlen_q`` sizes the grid
+    (any value is safe: CTAs stride over query tiles); ``max_seqlen_k`` is unused; ``arch`` is
+    accepted and ignored (only sm_100a kernels exist).
+
+    Extensions (keyword-only): ``softmax_scale`` (default 1/head_dim, the scale the reference
+    kernel hard-codes, triton_kernel.py:55), ``causal_align`` ("reference": mask diagonal at
+    local positions and bias offset sq - sk, reference.py:28-37; "bottom_right": both offset by
+    sk - sq, the flash-attention convention for chunked prefill and decode), ``out``.
+
+    Returns ``out`` [total_q, n_heads, 128] bf16.  Rows with no visible key are 0.
+    """
+    return _ops.prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                        max_seqlen_k, rel_extent, causal=causal, window_size=window_size,
+                        n_heads=n_heads, kv_heads=kv_heads, head_dim=head_dim,
+                        softmax_scale=softmax_scale, causal_align=causal_align, out=out)
+
+
+__all__ = ["inkling_fa4_rel_attention_triton"]

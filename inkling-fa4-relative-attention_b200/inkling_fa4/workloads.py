@@ -37,10 +37,12 @@ class Case:
         return max(self.seqlens_k) if self.seqlens_k else 0
 
 
-def _randn(shape, seed, std=1.0, dtype=torch.bfloat16):
-    g = torch.Generator(device="cpu")
+def _randn(shape, seed, std=1.0, dtype=torch.bfloat16, gen_device="cpu"):
+    """N(0, std^2) draws from a generator seeded per tensor.  ``gen_device="cuda"`` draws on
+    the GPU (fast for benchmark-size tensors; a different stream of numbers than the CPU)."""
+    g = torch.Generator(device=gen_device)
     g.manual_seed(int(seed))
-    x = torch.randn(*shape, generator=g, dtype=torch.float32)
+    x = torch.randn(*shape, generator=g, dtype=torch.float32, device=gen_device)
     if std != 1.0:
         x = x * std
     return x.to(dtype)
@@ -55,7 +57,7 @@ def cu_from_lens(lens) -> torch.Tensor:
 
 def make_case(seqlens_q, seqlens_k, n_heads, kv_heads, rel_extent, seed=0,
               device="cpu", dtype=torch.bfloat16, rel_std=1.0, head_dim=HEAD_DIM,
-              rel_per_head_table=False) -> Case:
+              rel_per_head_table=False, gen_device="cpu") -> Case:
     """Build one varlen case.  ``rel_std=1.0`` matches the reference tests (``torch.randn``,
     tests/test_correctness.py:11-20); the benchmark configurations use 0.5.
 
@@ -63,14 +65,16 @@ def make_case(seqlens_q, seqlens_k, n_heads, kv_heads, rel_extent, seed=0,
     ``[Tq, Hq, R]`` view with token stride 0.
     """
     tq, tk = int(sum(seqlens_q)), int(sum(seqlens_k))
-    q = _randn((tq, n_heads, head_dim), seed * 7 + 1, dtype=dtype)
-    k = _randn((tk, kv_heads, head_dim), seed * 7 + 2, dtype=dtype)
-    v = _randn((tk, kv_heads, head_dim), seed * 7 + 3, dtype=dtype)
+    gd = gen_device
+    q = _randn((tq, n_heads, head_dim), seed * 7 + 1, dtype=dtype, gen_device=gd)
+    k = _randn((tk, kv_heads, head_dim), seed * 7 + 2, dtype=dtype, gen_device=gd)
+    v = _randn((tk, kv_heads, head_dim), seed * 7 + 3, dtype=dtype, gen_device=gd)
     if rel_per_head_table:
-        table = _randn((n_heads, rel_extent), seed * 7 + 4, std=rel_std, dtype=dtype)
+        table = _randn((n_heads, rel_extent), seed * 7 + 4, std=rel_std, dtype=dtype, gen_device=gd)
         rel = table.to(device).unsqueeze(0).expand(tq, n_heads, rel_extent)
     else:
-        rel = _randn((tq, n_heads, rel_extent), seed * 7 + 4, std=rel_std, dtype=dtype).to(device)
+        rel = _randn((tq, n_heads, rel_extent), seed * 7 + 4, std=rel_std, dtype=dtype,
+                     gen_device=gd).to(device)
     return Case(q=q.to(device), k=k.to(device), v=v.to(device), rel=rel,
                 cu_q=cu_from_lens(seqlens_q).to(device), cu_k=cu_from_lens(seqlens_k).to(device),
                 seqlens_q=list(map(int, seqlens_q)), seqlens_k=list(map(int, seqlens_k)),
@@ -94,36 +98,39 @@ def config_cpu_reference(device="cpu", seed=0) -> Case:
     return c
 
 
-def config_ragged(device="cpu", seed=0, n=16, lo=1, hi=4096) -> Case:
+def config_ragged(device="cpu", seed=0, n=16, lo=1, hi=4096, gen_device="cpu") -> Case:
     """Config 2: 16 sequences with lengths ~ U[1, 4096], GQA 32/8, R=128."""
     lens = ragged_lengths(n, lo, hi, seed + 1000)
-    c = make_case(lens, lens, 32, 8, 128, seed=seed, device=device, rel_std=0.5)
+    c = make_case(lens, lens, 32, 8, 128, seed=seed, device=device, rel_std=0.5,
+                  gen_device=gen_device)
     c.meta.update(name="ragged16_u1_4096_gqa32_8", causal=True)
     return c
 
 
-def config_long(device="cpu", seed=0, seq=32768, window=None) -> Case:
+def config_long(device="cpu", seed=0, seq=32768, window=None, gen_device="cpu") -> Case:
     """Config 3: B=1, S=32768, GQA 32/8, R=128, full causal or window_left=4096."""
-    c = make_case([seq], [seq], 32, 8, 128, seed=seed, device=device, rel_std=0.5)
+    c = make_case([seq], [seq], 32, 8, 128, seed=seed, device=device, rel_std=0.5,
+                  gen_device=gen_device)
     c.meta.update(name=f"causal{seq}" + (f"_window{window}" if window is not None else ""),
                   causal=True, window_left=window)
     return c
 
 
-def config_chunked(device="cpu", seed=0, n=8, cache=16384, chunk=2048) -> Case:
+def config_chunked(device="cpu", seed=0, n=8, cache=16384, chunk=2048, gen_device="cpu") -> Case:
     """Config 4: 8 sequences of 16384 cached K/V tokens plus a 2048-token query chunk
     (bottom-right alignment: query i sits at position cache + i)."""
     c = make_case([chunk] * n, [cache + chunk] * n, 32, 8, 128, seed=seed, device=device,
-                  rel_std=0.5)
+                  rel_std=0.5, gen_device=gen_device)
     c.meta.update(name=f"chunked{n}x{cache}+{chunk}", causal=True, causal_align="bottom_right")
     return c
 
 
-def config_decode(device="cpu", seed=0, batch=128, lo=1024, hi=32768) -> Case:
+def config_decode(device="cpu", seed=0, batch=128, lo=1024, hi=32768, gen_device="cpu") -> Case:
     """Config 5: batch=128 single-token decode, KV lengths ~ U[1024, 32768], GQA 32/8, R=128,
     bottom-right alignment (the query is the last position of its sequence)."""
     lens = ragged_lengths(batch, lo, hi, seed + 2000)
-    c = make_case([1] * batch, lens, 32, 8, 128, seed=seed, device=device, rel_std=0.5)
+    c = make_case([1] * batch, lens, 32, 8, 128, seed=seed, device=device, rel_std=0.5,
+                  gen_device=gen_device)
     c.meta.update(name=f"decode{batch}_u{lo}_{hi}", causal=True, causal_align="bottom_right")
     return c
 

@@ -6,4 +6,6 @@ from .rel_attn_oracle import (  # noqa: F401
     bf16_bits_to_f32,
     f32_to_bf16_bits,
     alignment_offsets,
+    rel_attn_torch,
+    rel_attn_rows_torch,
 )

@@ -42,6 +42,8 @@ __all__ = [
     "bf16_bits_to_f32",
     "f32_to_bf16_bits",
     "alignment_offsets",
+    "rel_attn_torch",
+    "rel_attn_rows_torch",
 ]
 
 
@@ -152,4 +154,58 @@ def rel_attn(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, scale, rel_extent,
                     causal_align)
     if out_bf16:
         out = round_to_bf16(out)
+    return out
+
+
+def rel_attn_rows_torch(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_extent,
+                        causal=True, window_left=None, causal_align="reference"):
+    """``rel_attn_rows`` with torch CPU tensors (float32), which runs the elementwise steps on
+    all intra-op threads.  Same steps, same citations (reference.py:27-39)."""
+    import torch
+
+    mask_shift, bias_shift = alignment_offsets(sq, sk, causal_align)
+    scores = (q_rows @ k_b.T) * scale
+    qp = q_pos.view(-1, 1).to(torch.int64)
+    kp = torch.arange(sk, dtype=torch.int64).view(1, -1)
+    rel_dist = (qp + bias_shift) - kp
+    in_range = (rel_dist >= 0) & (rel_dist < rel_extent)
+    bias = torch.gather(rel_rows[:, :rel_extent], 1, rel_dist.clamp(0, rel_extent - 1))
+    scores = scores + torch.where(in_range, bias, torch.zeros((), dtype=bias.dtype))
+    if causal:
+        scores = scores.masked_fill(~(qp + mask_shift >= kp), float("-inf"))
+    if window_left is not None:
+        scores = scores.masked_fill(~((qp + mask_shift - kp) <= window_left), float("-inf"))
+    p = torch.softmax(scores, dim=-1)
+    return p @ v_b
+
+
+def rel_attn_torch(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, scale, rel_extent,
+                   causal=True, window_left=None, causal_align="reference", row_block=None,
+                   heads=None):
+    """Torch-CPU twin of :func:`rel_attn` (float32 in, float32 out)."""
+    import torch
+
+    q, k, v = q.float(), k.float(), v.float()
+    rel = rel_logits.float()
+    n_heads, kv_heads = q.shape[1], k.shape[1]
+    g = n_heads // kv_heads
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    cu_q = [int(x) for x in cu_seqlens_q]
+    cu_k = [int(x) for x in cu_seqlens_k]
+    for b in range(len(cu_q) - 1):
+        qs, qe, ks, ke = cu_q[b], cu_q[b + 1], cu_k[b], cu_k[b + 1]
+        sq, sk = qe - qs, ke - ks
+        if sq == 0:
+            continue
+        blk = sq if not row_block else row_block
+        for h in (range(n_heads) if heads is None else heads):
+            kh = h // g
+            k_b = k[ks:ke, kh].contiguous()
+            v_b = v[ks:ke, kh].contiguous()
+            for r0 in range(0, sq, blk):
+                r1 = min(sq, r0 + blk)
+                out[qs + r0:qs + r1, h] = rel_attn_rows_torch(
+                    q[qs + r0:qs + r1, h], k_b, v_b, rel[qs + r0:qs + r1, h],
+                    torch.arange(r0, r1), sq, sk, scale, rel_extent, causal, window_left,
+                    causal_align)
     return out

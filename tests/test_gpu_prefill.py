@@ -1,0 +1,152 @@
+"""Prefill parity on the B200: the sm_100a kernel, called through the drop-in API (and thus the
+C ABI), against the reference's golden outputs and the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import load_case, names
+from gpu_util import (assert_close, device_status_ok, np32, oracle_full, oracle_rows,
+                      run_prefill, to_dev)
+from inkling_fa4 import inkling_fa4_rel_attention_triton
+from inkling_fa4.triton_kernel_kv_pruned import inkling_fa4_rel_attention_kv_pruned_triton
+from inkling_fa4.workloads import (config_chunked, config_long, config_ragged, make_case)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    yield
+    assert device_status_ok(), "a kernel abandoned a bounded wait"
+
+
+@pytest.mark.parametrize("name", names())
+def test_golden_prefill(name):
+    """All reference test cases (tests/test_correctness.py:22-75) and the edge fixtures."""
+    spec, c, expected, _ = load_case(name)
+    c = to_dev(c)
+    c.q, c.k, c.v, c.rel = (t.to(torch.bfloat16) for t in (c.q, c.k, c.v, c.rel))
+    wl = spec["window_left"]
+    out = run_prefill(c, causal=spec["causal"], window_size=(-1 if wl is None else wl, 0),
+                      softmax_scale=spec["scale"])
+    torch.cuda.synchronize()
+    assert_close(np32(out), expected, what=name)
+
+
+def test_kv_pruned_alias_matches():
+    spec, c, expected, _ = load_case("sliding_window_h8_2")
+    c = to_dev(c)
+    out = inkling_fa4_rel_attention_kv_pruned_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 128,
+                                                     128, spec["rel_extent"],
+                                                     window_size=(spec["window_left"], 0))
+    assert_close(np32(out), expected)
+
+
+EDGE_LENS = [1, 17, 33, 127, 128, 129, 255, 256, 257, 300, 2]
+
+
+@pytest.mark.parametrize("heads", [(4, 4), (8, 2), (6, 2), (3, 1), (32, 8)])
+@pytest.mark.parametrize("causal,window", [(True, None), (False, None), (True, 70), (False, 33)])
+@pytest.mark.parametrize("rel_extent", [128, 1000])
+def test_ragged_edges_vs_oracle(heads, causal, window, rel_extent):
+    hq, hkv = heads
+    c = to_dev(make_case(EDGE_LENS, EDGE_LENS, hq, hkv, rel_extent, seed=hq * 7 + hkv))
+    out = run_prefill(c, causal=causal, window_size=(-1 if window is None else window, 0))
+    want = oracle_full(c, 1 / 128, causal=causal, window_left=window)
+    assert_close(np32(out), want)
+
+
+@pytest.mark.parametrize("align", ["reference", "bottom_right"])
+@pytest.mark.parametrize("window", [None, 100])
+def test_chunked_vs_oracle(align, window):
+    sq, sk = [130, 64, 1, 200], [300, 64, 257, 200]
+    c = to_dev(make_case(sq, sk, 8, 2, 128, seed=11))
+    out = run_prefill(c, causal_align=align, window_size=(-1 if window is None else window, 0))
+    want = oracle_full(c, 1 / 128, window_left=window, causal_align=align)
+    assert_close(np32(out), want)
+
+
+def test_chunked_bottom_right_equals_full_prefill_rows():
+    """north_star: chunked results agree with the corresponding full-prefill results."""
+    cache, chunk = 700, 333
+    full = to_dev(make_case([cache + chunk], [cache + chunk], 8, 2, 128, seed=3))
+    ref_rows = run_prefill(full)[cache:]
+    q, rel = full.q[cache:].contiguous(), full.rel[cache:].contiguous()
+    cu_q = torch.tensor([0, chunk], dtype=torch.int32, device="cuda")
+    got = inkling_fa4_rel_attention_triton(q, full.k, full.v, rel, cu_q, full.cu_k, chunk,
+                                           cache + chunk, 128, causal_align="bottom_right")
+    assert_close(np32(got), np32(ref_rows), atol=1e-2, rtol=1e-2)
+
+
+def test_stride0_per_head_table_and_sqrt_scale():
+    c = to_dev(make_case([200, 77], [200, 77], 8, 4, 128, seed=4, rel_per_head_table=True))
+    assert c.rel.stride(0) == 0
+    out = run_prefill(c, softmax_scale=128 ** -0.5)
+    assert_close(np32(out), oracle_full(c, 128 ** -0.5))
+
+
+def test_noncontiguous_inputs_and_out_param():
+    base = to_dev(make_case([150], [150], 8, 2, 64, seed=6))
+    # q as a head-slice of a wider tensor, k/v as token-strided views
+    wide = torch.zeros(150, 16, 128, dtype=torch.bfloat16, device="cuda")
+    wide[:, 4:12] = base.q
+    kk = torch.zeros(300, 2, 128, dtype=torch.bfloat16, device="cuda")
+    kk[::2] = base.k
+    vv = torch.zeros(150, 2, 256, dtype=torch.bfloat16, device="cuda")
+    vv[:, :, 64:192] = base.v
+    q, k, v = wide[:, 4:12], kk[::2], vv[:, :, 64:192]
+    out = torch.full((150, 8, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    r = inkling_fa4_rel_attention_triton(q, k, v, base.rel, base.cu_q, base.cu_k, 150, 150, 64,
+                                         out=out)
+    assert r.data_ptr() == out.data_ptr()
+    assert_close(np32(out), oracle_full(base, 1 / 128))
+
+
+def test_max_seqlen_hint_is_not_trusted_for_correctness():
+    c = to_dev(make_case([600, 40], [600, 40], 4, 2, 128, seed=8))
+    good = run_prefill(c)
+    bad = inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 1, 1, 128)
+    torch.testing.assert_close(bad, good, atol=0, rtol=0)
+
+
+def test_empty_keys_give_zero_rows():
+    c = to_dev(make_case([5, 40], [0, 40], 4, 4, 64, seed=9))
+    out = run_prefill(c)
+    assert torch.all(out[:5] == 0)
+    assert_close(np32(out[5:]), oracle_full(c, 1 / 128)[5:])
+
+
+def test_deterministic_across_calls():
+    c = to_dev(make_case([1000, 333], [1000, 333], 8, 2, 128, seed=10))
+    a, b = run_prefill(c), run_prefill(c)
+    torch.testing.assert_close(a, b, atol=0, rtol=0)
+
+
+# ---- benchmark configurations, checked on sampled rows (full-size) ---------------------
+
+def test_config_ragged_spot_rows():
+    c = to_dev(config_ragged())
+    out = run_prefill(c)
+    toks, want = oracle_rows(c, 6, list(range(0, 32, 5)), 1 / 128, seed=1)
+    got = np32(out[torch.as_tensor(toks, device="cuda")][:, list(range(0, 32, 5))])
+    assert_close(got, want)
+
+
+@pytest.mark.parametrize("window", [None, 4096])
+def test_config_32k_spot_rows(window):
+    c = to_dev(config_long(window=window))
+    out = run_prefill(c, window_size=(-1 if window is None else window, 0))
+    heads = [0, 13, 31]
+    toks, want = oracle_rows(c, 24, heads, 1 / 128, window_left=window, seed=2)
+    got = np32(out[torch.as_tensor(toks, device="cuda")][:, heads])
+    assert_close(got, want)
+    assert torch.isfinite(out.float()).all()
+
+
+def test_config_chunked_spot_rows():
+    c = to_dev(config_chunked())
+    out = run_prefill(c, causal_align="bottom_right")
+    heads = [1, 30]
+    toks, want = oracle_rows(c, 5, heads, 1 / 128, causal_align="bottom_right", seed=3)
+    got = np32(out[torch.as_tensor(toks, device="cuda")][:, heads])
+    assert_close(got, want)
