@@ -92,7 +92,7 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -240,7 +240,7 @@ def timed(fn, steps, warmup, stream, dist=None, barrier=None):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -248,7 +248,17 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-window", action="store_true")
+    ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
+                    help="prefill: headline + window only; decode: decode only (profiling runs)")
+    ap.add_argument("--prefill-seq", type=int, default=SEQ,
+                    help="sequence length of the prefill workload (32768 = BASELINE config 3)")
+    ap.add_argument("--decode-batch", type=int, default=128,
+                    help="decode batch (128 = BASELINE config 5)")
     args = ap.parse_args()
+    if args.only == "prefill":
+        args.no_decode = True
+    if args.only == "decode":
+        args.no_e2e = args.no_window = True
     if args.warmup < 3:
         args.warmup = 3
 
@@ -283,11 +293,12 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     # ---------------- headline: 32k causal prefill, inputs resident in HBM
-    c = config_long(device=dev, seed=rank, gen_device=dev)
-    flops = 4 * D * HQ * visible_pairs_causal(SEQ)
+    S = args.prefill_seq
+    c = config_long(device=dev, seed=rank, seq=S, gen_device=dev)
+    flops = 4 * D * HQ * visible_pairs_causal(S)
 
     def prefill_step():
-        return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, SEQ, SEQ, R)
+        return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R)
 
     uuids = []
     try:
@@ -295,10 +306,13 @@ def main():
     except Exception:
         pass
     sampler = ClockSampler(uuids) if rank == 0 else None
-    if sampler:
-        sampler.start()
-    ms = timed(prefill_step, args.steps, args.warmup, stream, dist, barrier)
-    clocks = sampler.stop() if sampler else None
+    if args.only == "decode":
+        ms, clocks = float("nan"), None
+    else:
+        if sampler:
+            sampler.start()
+        ms = timed(prefill_step, args.steps, args.warmup, stream, dist, barrier)
+        clocks = sampler.stop() if sampler else None
     ms_step = ms / args.steps
     value = world * flops * args.steps / (ms / 1e3) / 1e12
     achieved = flops / (ms_step / 1e3) / 1e12
@@ -310,18 +324,20 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) q/k/v and N(0,0.5) per-token rel logits, generated on "
                 "the device (rank r uses seed r)",
-        "config": {"workload": "causal32k_gqa32_8_d128_rel128", "batch": 1, "seq_len": SEQ,
+        "config": {"workload": ("causal32k_gqa32_8_d128_rel128" if S == SEQ else
+                                f"causal{S}_gqa32_8_d128_rel128"), "batch": 1, "seq_len": S,
                    "n_heads": HQ, "kv_heads": HKV, "head_dim": D, "rel_extent": R,
                    "causal": True, "window_left": None, "causal_align": "reference",
                    "flops_per_step_per_gpu": flops,
-                   "l2": "no flush; inputs of 671 MB per step exceed the 126 MB L2",
-                   "parallelism": f"{world} independent 32k sequences, one per rank (weak)"},
+                   "l2": (f"no flush; inputs of {(S * (HQ * (2 * D + 2 * R) + HKV * 4 * D)) >> 20} MB "
+                          "per step exceed the 126 MB L2"),
+                   "parallelism": f"{world} independent {S}-token sequences, one per rank (weak)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                      "peak_source": f"bf16_tflops (burst) of {peak_kind}",
                      "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                      "frac_of_datasheet_2250": achieved / 2250.0,
-                     "traffic": profile_traffic("prefill_causal32k_ncu.txt"),
+                     "traffic": profile_traffic("prefill_causal32k_ncu.txt") if S == SEQ else None,
                      "kernel": "rel_attn_prefill_kernel (1 launch per step)"},
         "gpu_launches": args.steps,
         "device_status": status,
@@ -333,7 +349,7 @@ def main():
     if not args.no_e2e:
         host = {n: getattr(c, n).cpu().pin_memory() for n in ("q", "k", "v", "rel", "cu_q", "cu_k")}
         dbuf = {n: torch.empty_like(getattr(c, n)) for n in host}
-        out_host = torch.empty((SEQ, HQ, D), dtype=torch.bfloat16).pin_memory()
+        out_host = torch.empty((S, HQ, D), dtype=torch.bfloat16).pin_memory()
         h2d = sum(t.numel() * t.element_size() for t in host.values())
         d2h = out_host.numel() * out_host.element_size()
 
@@ -341,7 +357,7 @@ def main():
             for n, t in host.items():
                 dbuf[n].copy_(t, non_blocking=True)
             o = inkling_fa4_rel_attention_triton(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["rel"],
-                                                 dbuf["cu_q"], dbuf["cu_k"], SEQ, SEQ, R)
+                                                 dbuf["cu_q"], dbuf["cu_k"], S, S, R)
             out_host.copy_(o, non_blocking=True)
 
         e_steps = max(3, min(args.steps, 10))
@@ -355,10 +371,10 @@ def main():
 
     # ---------------- sliding window 4096 at 32k (BASELINE config 3b)
     if not args.no_window:
-        wflops = 4 * D * HQ * visible_pairs_causal(SEQ, 4096)
+        wflops = 4 * D * HQ * visible_pairs_causal(S, 4096)
 
         def win_step():
-            return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, SEQ, SEQ,
+            return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S,
                                                     R, window_size=(4096, 0))
 
         wms = timed(win_step, args.steps, args.warmup, stream, dist, barrier)
@@ -370,7 +386,7 @@ def main():
 
     # ---------------- batched decode
     if not args.no_decode:
-        dc = config_decode(device=dev, seed=rank, gen_device=dev)
+        dc = config_decode(device=dev, seed=rank, batch=args.decode_batch, gen_device=dev)
         lens = dc.seqlens_k
         kv_bytes = sum(lens) * HKV * D * 2 * 2
         other = len(lens) * HQ * (D * 2 * 2 + R * 2)
@@ -399,7 +415,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": per_gpu / peaks["hbm_gbs"],
                          "peak_source": f"hbm_gbs of {peak_kind}",
-                         "traffic": profile_traffic("decode_b128_ncu.txt")},
+                         "traffic": (profile_traffic("decode_b128_ncu.txt")
+                                     if args.decode_batch == 128 else None)},
             "gpu_launches": args.steps * (2 if nsplit > 1 else 1)}
         del dc, ws
         torch.cuda.empty_cache()
@@ -407,7 +424,7 @@ def main():
     result["device_status"] = _lib.read_device_status(stream.cuda_stream)
 
     # ---------------- CPU baseline (rank 0, N = 1)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only == "all":
         v, cores, sample = cpu_baseline_prefill(args.cpu_seconds)
         result["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                                   "sample": sample}

@@ -1,0 +1,106 @@
+"""Multi-GPU sharding of the attention call (one process per GPU, torch.distributed).
+
+The path shards with no exchange during compute:
+
+* by KV-head group: rank r of n owns kv heads [r*Hkv/n, (r+1)*Hkv/n) and their query heads
+  [r*Hq/n, (r+1)*Hq/n); it runs the kernels on head slices of q/k/v/rel (views, no copies:
+  the kernels take arbitrary head strides) for all sequences.  The only collective is the
+  optional all-gather of the output heads (``gather_heads``), over NCCL / NVLink.
+* by sequence: ``balance_sequences`` splits a ragged batch into n groups of nearly equal
+  token count (for decode, nearly equal KV bytes); each rank runs its sequences.
+
+Nothing here reads another GPU's memory; each rank's kernels only touch local tensors.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class HeadShard:
+    rank: int
+    world: int
+    kv_lo: int
+    kv_hi: int
+    q_lo: int
+    q_hi: int
+
+    @property
+    def n_q(self) -> int:
+        return self.q_hi - self.q_lo
+
+    @property
+    def n_kv(self) -> int:
+        return self.kv_hi - self.kv_lo
+
+
+def head_shard(n_heads: int, kv_heads: int, world: int, rank: int) -> HeadShard:
+    """KV-head-group shard of rank ``rank`` (GQA groups are never split)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} / world {world}")
+    if n_heads % kv_heads:
+        raise ValueError("n_heads must be a multiple of kv_heads")
+    if kv_heads % world:
+        raise ValueError(f"kv_heads {kv_heads} not divisible by world size {world}")
+    g = n_heads // kv_heads
+    per = kv_heads // world
+    kv_lo = rank * per
+    return HeadShard(rank, world, kv_lo, kv_lo + per, kv_lo * g, (kv_lo + per) * g)
+
+
+def shard_tensors(sh: HeadShard, q, k, v, rel):
+    """Head-slice views of the inputs for one rank."""
+    return (q[:, sh.q_lo:sh.q_hi], k[:, sh.kv_lo:sh.kv_hi], v[:, sh.kv_lo:sh.kv_hi],
+            rel[:, sh.q_lo:sh.q_hi])
+
+
+def gather_heads(out_shard: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """All-gather per-rank outputs [T, Hq/n, d] into the full [T, Hq, d] (rank-ordered head
+    blocks).  NCCL uses one all_gather_into_tensor; other backends fall back to all_gather."""
+    import torch.distributed as dist
+
+    t, hs, d = out_shard.shape
+    src = out_shard.contiguous()
+    if dist.get_backend(group) == "nccl":
+        buf = torch.empty((world, t, hs, d), dtype=src.dtype, device=src.device)
+        dist.all_gather_into_tensor(buf, src, group=group)
+    else:
+        parts = [torch.empty_like(src) for _ in range(world)]
+        dist.all_gather(parts, src, group=group)
+        buf = torch.stack(parts)
+    return buf.permute(1, 0, 2, 3).reshape(t, world * hs, d)
+
+
+def balance_sequences(lengths, world: int, weights=None):
+    """Greedy longest-first assignment of sequences to ``world`` ranks by weight (default:
+    length).  Returns, per rank, the sorted list of sequence indices."""
+    w = list(lengths if weights is None else weights)
+    order = sorted(range(len(w)), key=lambda i: -w[i])
+    load = [0] * world
+    groups = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda j: (load[j], j))
+        groups[r].append(i)
+        load[r] += w[i]
+    return [sorted(g) for g in groups]
+
+
+def select_sequences(idx, cu_q, cu_k, *tensors_q_k):
+    """Pack the chosen sequences into contiguous varlen tensors.  ``tensors_q_k`` is
+    (q, rel, k, v); returns (q, rel, k, v, cu_q, cu_k) for the subset (host-side index
+    arithmetic; the copies run on the tensors' device)."""
+    q, rel, k, v = tensors_q_k
+    cq = [int(x) for x in cu_q.tolist()]
+    ck = [int(x) for x in cu_k.tolist()]
+    rows_q = torch.cat([torch.arange(cq[i], cq[i + 1]) for i in idx]) if idx else torch.zeros(0, dtype=torch.long)
+    rows_k = torch.cat([torch.arange(ck[i], ck[i + 1]) for i in idx]) if idx else torch.zeros(0, dtype=torch.long)
+    lq = [cq[i + 1] - cq[i] for i in idx]
+    lk = [ck[i + 1] - ck[i] for i in idx]
+    new_cq = torch.tensor([0] + list(torch.tensor(lq).cumsum(0).tolist() if lq else []), dtype=torch.int32)
+    new_ck = torch.tensor([0] + list(torch.tensor(lk).cumsum(0).tolist() if lk else []), dtype=torch.int32)
+    dev = q.device
+    rq, rk = rows_q.to(dev), rows_k.to(dev)
+    return (q.index_select(0, rq), rel.index_select(0, rq), k.index_select(0, rk),
+            v.index_select(0, rk), new_cq.to(dev), new_ck.to(dev))

@@ -91,6 +91,8 @@ def rel_attn_rows(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_extent,
     ``q_pos`` [n] local query positions.  Returns float32 [n, d].
     Follows reference.py:27-39 row by row.
     """
+    if sk == 0:  # softmax over an empty key axis: the reference's einsum yields zeros
+        return np.zeros((q_rows.shape[0], v_b.shape[1]), dtype=np.float32)
     mask_shift, bias_shift = alignment_offsets(sq, sk, causal_align)
     scores = (q_rows @ k_b.T) * np.float32(scale)                       # reference.py:27
     qp = q_pos.reshape(-1, 1).astype(np.int64)
@@ -163,6 +165,8 @@ def rel_attn_rows_torch(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_ex
     all intra-op threads.  Same steps, same citations (reference.py:27-39)."""
     import torch
 
+    if sk == 0:
+        return torch.zeros((q_rows.shape[0], v_b.shape[1]), dtype=torch.float32)
     mask_shift, bias_shift = alignment_offsets(sq, sk, causal_align)
     scores = (q_rows @ k_b.T) * scale
     qp = q_pos.view(-1, 1).to(torch.int64)

@@ -64,6 +64,7 @@ def golden_cases():
     cases.append(("per_head_table_h4_4", dict(sq=[200], sk=[200], heads=(4, 4), rel_extent=128, per_head_table=True, rel_std=0.5)))
     cases.append(("cpu_config1_f32", dict(sq=[128], sk=[128], heads=(4, 4), rel_extent=128, per_head_table=True,
                                           rel_std=0.5, scale=128 ** -0.5, dtype="f32")))
+    cases.append(("empty_keys_h4_2", dict(sq=[5, 40, 3], sk=[0, 40, 0], heads=(4, 2), rel_extent=64)))
     for i, (name, spec) in enumerate(cases):
         spec.setdefault("seed", 100 + i)
         spec.setdefault("scale", 1.0 / 128)

@@ -79,7 +79,7 @@ def test_chunked_bottom_right_equals_full_prefill_rows():
 
 
 def test_stride0_per_head_table_and_sqrt_scale():
-    c = to_dev(make_case([200, 77], [200, 77], 8, 4, 128, seed=4, rel_per_head_table=True))
+    c = make_case([200, 77], [200, 77], 8, 4, 128, seed=4, rel_per_head_table=True, device="cuda")
     assert c.rel.stride(0) == 0
     out = run_prefill(c, softmax_scale=128 ** -0.5)
     assert_close(np32(out), oracle_full(c, 128 ** -0.5))
