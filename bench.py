@@ -248,10 +248,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-window", action="store_true")
+    ap.add_argument("--extra-configs", action="store_true",
+                    help="also time BASELINE configs 2 (ragged) and 4 (chunked)")
     ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
                     help="prefill: headline + window only; decode: decode only (profiling runs)")
     ap.add_argument("--prefill-seq", type=int, default=SEQ,
                     help="sequence length of the prefill workload (32768 = BASELINE config 3)")
+    ap.add_argument("--tile-config", type=int, default=0,
+                    help="prefill kernel variant (0 = default; see autotune_configs)")
     ap.add_argument("--decode-batch", type=int, default=128,
                     help="decode batch (128 = BASELINE config 5)")
     args = ap.parse_args()
@@ -297,7 +301,12 @@ def main():
     c = config_long(device=dev, seed=rank, seq=S, gen_device=dev)
     flops = 4 * D * HQ * visible_pairs_causal(S)
 
+    from inkling_fa4 import _ops
+
     def prefill_step():
+        if args.tile_config:
+            return _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R,
+                                tile_config=args.tile_config)
         return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R)
 
     uuids = []
@@ -338,7 +347,8 @@ def main():
                      "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                      "frac_of_datasheet_2250": achieved / 2250.0,
                      "traffic": profile_traffic("prefill_causal32k_ncu.txt") if S == SEQ else None,
-                     "kernel": "rel_attn_prefill_kernel (1 launch per step)"},
+                     "kernel": "rel_attn_prefill_kernel (1 launch per step)",
+                     "tile_config": args.tile_config},
         "gpu_launches": args.steps,
         "device_status": status,
     }
@@ -346,28 +356,74 @@ def main():
         result["clocks"] = clocks
 
     # ---------------- end to end through the public API with host buffers
+    # Every step uploads its own inputs from pinned host memory, runs the public API call and
+    # downloads its output to pinned host memory.  Three streams and two buffer sets let the
+    # upload of step i+1 and the download of step i-1 overlap the kernel of step i, as a
+    # serving pipeline would; the timed region spans the first upload to the last download.
     if not args.no_e2e:
-        host = {n: getattr(c, n).cpu().pin_memory() for n in ("q", "k", "v", "rel", "cu_q", "cu_k")}
-        dbuf = {n: torch.empty_like(getattr(c, n)) for n in host}
-        out_host = torch.empty((S, HQ, D), dtype=torch.bfloat16).pin_memory()
+        names = ("q", "k", "v", "rel", "cu_q", "cu_k")
+        host = {n: getattr(c, n).cpu().pin_memory() for n in names}
+        dbuf = [{n: torch.empty_like(getattr(c, n)) for n in names} for _ in range(2)]
+        dout = [torch.empty((S, HQ, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        hout = [torch.empty((S, HQ, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
         h2d = sum(t.numel() * t.element_size() for t in host.values())
-        d2h = out_host.numel() * out_host.element_size()
+        d2h = hout[0].numel() * hout[0].element_size()
+        s_up, s_run, s_down = (torch.cuda.Stream(dev) for _ in range(3))
+        ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("up", "run", "down")}
+        e_steps = max(4, min(args.steps, 20))
 
-        def e2e_step():
-            for n, t in host.items():
-                dbuf[n].copy_(t, non_blocking=True)
-            o = inkling_fa4_rel_attention_triton(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["rel"],
-                                                 dbuf["cu_q"], dbuf["cu_k"], S, S, R)
-            out_host.copy_(o, non_blocking=True)
+        def pipeline(nsteps):
+            for i in range(nsteps):
+                b = i % 2
+                with torch.cuda.stream(s_up):
+                    if i >= 2:
+                        s_up.wait_event(ev["run"][b])      # kernel i-2 done with dbuf[b]
+                    for n in names:
+                        dbuf[b][n].copy_(host[n], non_blocking=True)
+                    ev["up"][b].record(s_up)
+                with torch.cuda.stream(s_run):
+                    s_run.wait_event(ev["up"][b])
+                    if i >= 2:
+                        s_run.wait_event(ev["down"][b])    # download i-2 done with dout[b]
+                    d = dbuf[b]
+                    inkling_fa4_rel_attention_triton(d["q"], d["k"], d["v"], d["rel"], d["cu_q"],
+                                                     d["cu_k"], S, S, R, out=dout[b])
+                    ev["run"][b].record(s_run)
+                with torch.cuda.stream(s_down):
+                    s_down.wait_event(ev["run"][b])
+                    hout[b].copy_(dout[b], non_blocking=True)
+                    ev["down"][b].record(s_down)
+            for st in (s_up, s_run, s_down):
+                stream.wait_stream(st)
 
-        e_steps = max(3, min(args.steps, 10))
-        ems = timed(e2e_step, e_steps, 2, stream, dist, barrier)
+        pipeline(2)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for st in (s_up, s_run, s_down):
+            st.wait_stream(stream)
+        pipeline(e_steps)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        ems = t0.elapsed_time(t1)
+        if dist is not None:
+            tt = torch.tensor([ems], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ems = float(tt.item())
+        ok = torch.equal(hout[(e_steps - 1) % 2], dout[(e_steps - 1) % 2].cpu())
         result["e2e"] = {"value": world * flops * e_steps / (ems / 1e3) / 1e12, "unit": "TFLOP/s",
                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                         "ms_per_step": ems / e_steps,
-                         "path": "pinned host -> device copies, inkling_fa4_rel_attention_triton "
-                                 "(C ABI), device -> pinned host copy of the output, one stream"}
-        del host, dbuf, out_host
+                         "ms_per_step": ems / e_steps, "steps": e_steps,
+                         "output_roundtrip_ok": bool(ok),
+                         "path": "pinned host -> device upload of q/k/v/rel/cu_seqlens, "
+                                 "inkling_fa4_rel_attention_triton (C ABI), device -> pinned host "
+                                 "download of the output; 3 streams, 2 buffer sets, every step "
+                                 "moves its own inputs and output"}
+        del host, dbuf, dout, hout
 
     # ---------------- sliding window 4096 at 32k (BASELINE config 3b)
     if not args.no_window:
@@ -383,6 +439,29 @@ def main():
                                "window_left": 4096, "flops_per_step_per_gpu": wflops}
     del c
     torch.cuda.empty_cache()
+
+    # ---------------- ragged (config 2) and chunked (config 4) prefill, on request
+    if args.extra_configs:
+        from inkling_fa4.workloads import causal_visible_pairs, config_chunked, config_ragged
+
+        for name, make, align in (("ragged", config_ragged, "reference"),
+                                  ("chunked", config_chunked, "bottom_right")):
+            cc = make(device=dev, seed=rank, gen_device=dev)
+            fl = 4 * D * HQ * causal_visible_pairs(cc.seqlens_q, cc.seqlens_k,
+                                                   causal_align=align)
+
+            def step(cc=cc, align=align):
+                return inkling_fa4_rel_attention_triton(cc.q, cc.k, cc.v, cc.rel, cc.cu_q,
+                                                        cc.cu_k, cc.max_q, cc.max_k, R,
+                                                        causal_align=align)
+
+            xms = timed(step, args.steps, args.warmup, stream, dist, barrier)
+            result[name] = {"value": world * fl * args.steps / (xms / 1e3) / 1e12,
+                            "unit": "TFLOP/s", "ms_per_step": xms / args.steps,
+                            "flops_per_step_per_gpu": fl, "causal_align": align,
+                            "seqlens_q": cc.seqlens_q if name == "ragged" else None}
+            del cc
+        torch.cuda.empty_cache()
 
     # ---------------- batched decode
     if not args.no_decode:

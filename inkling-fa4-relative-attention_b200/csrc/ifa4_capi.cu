@@ -168,19 +168,19 @@ const char* ifa4_last_error_string(void) { return g_last_error; }
 int32_t ifa4_abi_version(void) { return IFA4_ABI_VERSION; }
 
 const char* ifa4_prefill_tile_config_name(int32_t tile_config) {
-  switch (tile_config) {
-    case 0:
-      return "sm100_q2x128_kv128_d128_tmem512_ws12";
-    default:
-      return "";
-  }
+  static const char* names[ifa4::kPrefillNumTileConfigs] = {
+      "sm100_q2x128_kv128_d128_ws12_default", "sm100_q2x128_kv128_d128_ws12_emu0of16",
+      "sm100_q2x128_kv128_d128_ws12_emu2of16", "sm100_q2x128_kv128_d128_ws12_emu4of16",
+      "sm100_q2x128_kv128_d128_ws12_emu6of16", "sm100_q2x128_kv128_d128_ws12_emu8of16"};
+  if (tile_config < 0 || tile_config >= ifa4::kPrefillNumTileConfigs) return "";
+  return names[tile_config];
 }
 
 int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   g_last_error[0] = '\0';
   int rc = validate_common(p, "prefill");
   if (rc) return rc;
-  if (p->tile_config != 0)
+  if (ifa4::prefill_emulated_exp_columns(p->tile_config) < 0)
     return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d unknown", p->tile_config);
   if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
   if (p->total_k == 0) {
@@ -229,7 +229,7 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   if (slots < 1) slots = 1;
   if (slots > 65535) slots = 65535;
   cudaError_t e = ifa4::launch_prefill_sm100(a, tq, tk, tv, static_cast<int>(slots),
-                                             static_cast<cudaStream_t>(stream));
+                                             p->tile_config, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return IFA4_OK;
 }

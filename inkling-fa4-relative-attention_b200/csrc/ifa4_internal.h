@@ -33,10 +33,17 @@ struct PrefillLaunch {
   int smem_bytes;
 };
 
-// Builds nothing; launches the tcgen05 prefill kernel.  Returns a cudaError_t.
+// Prefill tile configurations: the kernel variants differ in how many of every 16 score
+// columns get their exponential from the FMA-pipe polynomial instead of the SFU.
+// tile_config 0 = default, 1..5 = 0, 2, 4, 6, 8 emulated columns of 16.
+constexpr int kPrefillDefaultEmu = 0;
+constexpr int kPrefillNumTileConfigs = 6;
+int prefill_emulated_exp_columns(int tile_config);  // -1 for an unknown id
+
+// Launches the tcgen05 prefill kernel variant of `tile_config`.  Returns a cudaError_t.
 cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                 int q_slots, cudaStream_t stream);
+                                 int q_slots, int tile_config, cudaStream_t stream);
 
 struct DecodeKernelArgs {
   const uint16_t* q;

@@ -50,6 +50,16 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;                // log2 units: rescale O at 256x
 
+// Register split: warpgroup 0 (producer, MMA issuer, TMEM owner, spare) drops to kRegsCtl,
+// the two softmax warpgroups rise to kRegsSoftmax.  4*32*kRegsCtl + 8*32*kRegsSoftmax must not
+// exceed the 384 * kLaunchRegs registers the CTA is launched with, or setmaxnreg.inc would wait
+// forever; inkling_fa4/build.py fails the build unless ptxas reports exactly kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsCtl = 64;
+constexpr int kRegsSoftmax = 216;
+static_assert(4 * 32 * kRegsCtl + 8 * 32 * kRegsSoftmax <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
+
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
 
@@ -113,23 +123,26 @@ __device__ __forceinline__ TileInfo tile_info(const PrefillKernelArgs& a, int qt
 }
 
 __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr) {
+  const uint64_t qd = sdesc_sw128(q_addr, 16, 1024);
+  const uint64_t kd = sdesc_sw128(k_addr, 16, 1024);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
     const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-    umma_ss(tmem_s, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-            kIdescQK, kk > 0 ? 1u : 0u);
+    umma_ss(tmem_s, sdesc_advance(qd, off), sdesc_advance(kd, off), kIdescQK, kk > 0 ? 1u : 0u);
   }
 }
 
 __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_addr,
                                          bool accumulate) {
+  const uint64_t vd = sdesc_sw128(v_addr, kHalf, 1024);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    umma_ts(tmem_o, tmem_p + kk * 8, sdesc_sw128(v_addr + kk * 2048, kHalf, 1024), kIdescPV,
+    umma_ts(tmem_o, tmem_p + kk * 8, sdesc_advance(vd, kk * 2048), kIdescPV,
             (kk > 0 || accumulate) ? 1u : 0u);
   }
 }
 
+template <int kEmu>
 __global__ void __launch_bounds__(kThreads, 1)
     rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
                             const __grid_constant__ CUtensorMap tm_q,
@@ -183,8 +196,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
   const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
-
-  if (warp == 0) {
+  if (warp < 4) {
+   regs_dec<kRegsCtl>();
+   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t qc = 0, kc = 0, vc = 0;
@@ -234,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&bars->v_full[last & 1], (last >> 1) & 1, ab);
       }
     }
-  } else if (warp == 1) {
+   } else if (warp == 1) {
     // ------------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
       uint32_t qc = 0, kc = 0, vc = 0, pc = 0, oc = 0;
@@ -302,7 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, ab);
     }
-  } else if (warp >= 4) {
+   }
+  } else {
+    regs_inc<kRegsSoftmax>();
     // ------------------------------------------------------------------ softmax
     const int s = (warp - 4) >> 2;
     const int row = (warp & 3) * 32 + lane;
@@ -341,39 +357,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait_warp(&bars->s_full[s], pc & 1, ab))) break;
         ++pc;
         tc_fence_after();
-        uint32_t r[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
-        tmem_wait_ld();
         float x[128];
+        {
+          uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
+          tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[c][i]) * a.scale_log2;
-
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[c][i]);
+        }
         const int k0 = (t.j_lo + j) * kBN;
         // relative bias: keys in [dmax - R + 1, dmax] carry rel[row, dmax - key]
         const int bl = dmax - a.rel_extent + 1 - k0;  // first column with bias
         const int bh = dmax - k0;                     // last column with bias
-        if (row_valid && bl <= 127 && bh >= 0) {
+        const int cl = key_lo - k0, ch = key_hi - k0;  // visible columns [cl, ch)
+        const bool has_bias = row_valid && bl <= 127 && bh >= 0;
+        const bool has_mask = cl > 0 || ch < kBN;
+        // Interior rows keep raw scores (the scale is folded into the exponent FMA); rows with
+        // bias or mask turn x into the scaled, biased, masked logit first.
+        float mul = a.scale_log2;
+        if (has_bias || has_mask) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) {
-            if (c >= bl && c <= bh) {
-              const uint16_t bits = __ldg(rel_row + (bh - c));
-              x[c] += bf16_bits_to_float(bits) * kLog2e;
+          for (int c = 0; c < 128; ++c) x[c] *= a.scale_log2;
+          if (has_bias) {
+#pragma unroll
+            for (int c = 0; c < 128; ++c) {
+              if (c >= bl && c <= bh) {
+                const uint16_t bits = __ldg(rel_row + (bh - c));
+                x[c] += bf16_bits_to_float(bits) * kLog2e;
+              }
             }
           }
-        }
-        // mask: only rows whose visible range does not cover the whole tile
-        const int cl = key_lo - k0, ch = key_hi - k0;  // visible columns [cl, ch)
-        if (cl > 0 || ch < kBN) {
+          if (has_mask) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (c < cl || c >= ch) x[c] = -INFINITY;
+            for (int c = 0; c < 128; ++c)
+              if (c < cl || c >= ch) x[c] = -INFINITY;
+          }
+          mul = 1.f;
         }
-        float m_tile = x[0];
+        // row max: four independent chains of 3-input max
+        float mA = x[0], mB = x[1], mC = x[2], mD = x[3];
 #pragma unroll
-        for (int c = 1; c < 128; ++c) m_tile = fmaxf(m_tile, x[c]);
+        for (int c = 4; c < 128; c += 8) {
+          mA = fmax3(mA, x[c], x[c + 1]);
+          mB = fmax3(mB, x[c + 2], x[c + 3]);
+          mC = fmax3(mC, x[c + 4], x[c + 5]);
+          mD = fmax3(mD, x[c + 6], x[c + 7]);
+        }
+        const float m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
         const float m_new = fmaxf(m_run, m_tile);
         float alpha = 1.f;
         bool need_rescale = false;
@@ -386,20 +419,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_run = m_new;
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        float lsum = 0.f;
+        // p = 2^(x * mul - m_use): kEmu of every 16 columns on the FMA pipe, the rest on the SFU
+        const uint64_t mul2 = f2_pack(mul, mul);
+        const uint64_t neg2 = f2_pack(-m_use, -m_use);
+        uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = fast_exp2(x[c * 32 + 2 * i] - m_use);
-            const float p1 = fast_exp2(x[c * 32 + 2 * i + 1] - m_use);
-            lsum += p0 + p1;
+            const int col = c * 32 + 2 * i;
+            float y0, y1;
+            f2_unpack(f2_fma(f2_pack(x[col], x[col + 1]), mul2, neg2), y0, y1);
+            float p0, p1;
+            if ((col & 15) < kEmu) {
+              exp2_poly_pair(y0, y1, p0, p1);
+            } else {
+              p0 = fast_exp2(y0);
+              p1 = fast_exp2(y1);
+            }
+            acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
             pk[i] = pack_bf16x2(p0, p1);
           }
           tmem_st16(t_s + c * 16, pk);
         }
-        l_run += lsum;
+        {
+          const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+          float u0, u1;
+          f2_unpack(f2_add(a01, a23), u0, u1);
+          l_run += u0 + u1;
+        }
         // Conditional O correction (PV of the previous tile is complete: its commit
         // preceded this tile's S commit).
         if (__any_sync(0xffffffffu, need_rescale)) {
@@ -422,7 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait_warp(&bars->o_full[s], oc & 1, ab))) break;
       ++oc;
       tc_fence_after();
-      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+      // a row that never saw a visible key outputs 0 (the FMA-pipe exp2 of a masked
+      // logit is ~2^-125, not 0, so l alone does not tell)
+      const float inv_l = (l_run > 0.f && m_run != -INFINITY) ? 1.f / l_run : 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -455,9 +506,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill
 
-cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
-                                 const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                 int q_slots, cudaStream_t stream) {
+namespace {
+template <int kEmu>
+cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
+                           const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
+                           cudaStream_t stream) {
   // The dynamic shared-memory limit is a per-device function attribute.
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -465,17 +518,43 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel,
+    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(prefill::kSmemAlloc));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
+  prefill::rel_attn_prefill_kernel<kEmu>
+      <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
+  return cudaGetLastError();
+}
+}  // namespace
+
+int prefill_emulated_exp_columns(int tile_config) {
+  switch (tile_config) {
+    case 0: return kPrefillDefaultEmu;
+    case 1: return 0;
+    case 2: return 2;
+    case 3: return 4;
+    case 4: return 6;
+    case 5: return 8;
+    default: return -1;
+  }
+}
+
+cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
+                                 const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                 int q_slots, int tile_config, cudaStream_t stream) {
   const int head_slots = args.pair_heads ? args.n_heads / 2 : args.n_heads;
   dim3 grid(head_slots, args.batch, q_slots);
-  prefill::rel_attn_prefill_kernel<<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(
-      args, tm_q, tm_k, tm_v);
-  return cudaGetLastError();
+  switch (prefill_emulated_exp_columns(tile_config)) {
+    case 0: return launch_variant<0>(args, tm_q, tm_k, tm_v, grid, stream);
+    case 2: return launch_variant<2>(args, tm_q, tm_k, tm_v, grid, stream);
+    case 4: return launch_variant<4>(args, tm_q, tm_k, tm_v, grid, stream);
+    case 6: return launch_variant<6>(args, tm_q, tm_k, tm_v, grid, stream);
+    case 8: return launch_variant<8>(args, tm_q, tm_k, tm_v, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace ifa4

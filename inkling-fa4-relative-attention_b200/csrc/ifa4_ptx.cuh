@@ -188,6 +188,17 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                : "memory");
 }
 
+// Warpgroup register re-balancing (all 128 threads of the warpgroup execute it).  The sum of the
+// warpgroups' new counts must not exceed what the CTA was launched with, or `inc` never returns.
+template <int kRegs>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -216,6 +227,16 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr, uint32_t lbo
   d |= static_cast<uint64_t>(1) << 46;
   d |= static_cast<uint64_t>(2) << 61;
   return d;
+}
+
+// Descriptor of the same matrix layout starting `off_bytes` further (off < 256 KB - start):
+// the start address is the low 14-bit field in 16-byte units, so the add cannot carry out of
+// it.  Volatile so the compiler re-derives it at each use instead of keeping every descriptor
+// of an unrolled loop live in registers.
+__device__ __forceinline__ uint64_t sdesc_advance(uint64_t desc, uint32_t off_bytes) {
+  uint64_t r;
+  asm volatile("add.u64 %0, %1, %2;" : "=l"(r) : "l"(desc), "l"(static_cast<uint64_t>(off_bytes >> 4)));
+  return r;
 }
 
 // Instruction descriptor, kind::f16, bf16 x bf16 -> f32, dense.
@@ -311,6 +332,64 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32 pairs (Blackwell f32x2 arithmetic): one instruction operates on two floats.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// max of three floats in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of floats on the FMA pipe instead of the SFU.
+// Range reduction (Cody-Waite for base 2 needs no split constant): n = round(x) obtained by
+// adding the rounding constant 1.5 * 2^23, f = x - n in [-1/2, 1/2]; 2^f by a degree-3
+// polynomial minimising the relative error on [-1/2, 1/2] (Remez exchange; max relative error
+// 7.5e-5, well under the 2^-9 half-ulp of the bf16 the result is rounded to); 2^n is applied by
+// adding n to the exponent field (bits(t) << 23 == n << 23 modulo 2^32 for t = 1.5 * 2^23 + n).
+// Inputs are clamped to >= -125 (the result is then ~2^-125 rather than 0) and must be <= 127.
+__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t r2 = f2_pack(kRound, kRound);
+  const uint64_t t = f2_add(x, r2);
+  const uint64_t f = f2_sub(x, f2_sub(t, r2));
+  uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f,
+                      f2_pack(0.2426111251f, 0.2426111251f));
+  p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
+  p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

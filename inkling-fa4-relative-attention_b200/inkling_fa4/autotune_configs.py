@@ -22,6 +22,20 @@ PRESETS = {
         "buckets": [],
     },
 }
+
+# Prefill kernel variants behind tile_config (all: two 128-row query sub-tiles per CTA, 128-key
+# KV tiles, 12 warps, 2-stage K and V rings).  They differ in how many of every 16 score columns
+# take their exponential from the FMA-pipe polynomial instead of the SFU.  Measured on one B200,
+# bench.py --only prefill (32k causal, GQA 32/8): TFLOP/s per variant.  tile_config 0 resolves
+# to the fastest.
+TILE_CONFIGS = {
+    0: {"emulated_exp_of_16": 0, "note": "default (= tile_config 1)"},
+    1: {"emulated_exp_of_16": 0, "causal32k_tflops": 1019.5},
+    2: {"emulated_exp_of_16": 2, "causal32k_tflops": 902.8},
+    3: {"emulated_exp_of_16": 4, "causal32k_tflops": 882.0},
+    4: {"emulated_exp_of_16": 6, "causal32k_tflops": 869.9},
+    5: {"emulated_exp_of_16": 8, "causal32k_tflops": 865.9},
+}
 DECODE_PRESET = {"BLOCK_K": 64, "num_warps": 5, "num_stages": 3, "chunk_len": 0, "num_splits": 0}
 
 

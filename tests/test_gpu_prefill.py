@@ -150,3 +150,31 @@ def test_config_chunked_spot_rows():
     toks, want = oracle_rows(c, 5, heads, 1 / 128, causal_align="bottom_right", seed=3)
     got = np32(out[torch.as_tensor(toks, device="cuda")][:, heads])
     assert_close(got, want)
+
+
+@pytest.mark.parametrize("tile_config", [1, 2, 3, 4, 5])
+def test_tile_config_variants_match_oracle(tile_config):
+    """Every kernel variant (fraction of exponentials computed on the FMA pipe) is correct,
+    including rows that see no key (must be 0, not the ~2^-125 of an emulated exp2(-inf))."""
+    from inkling_fa4 import _ops
+    c = to_dev(make_case([300, 17, 129, 5], [300, 17, 129, 0], 8, 2, 128, seed=12))
+    for causal, window in ((True, None), (True, 40), (False, None)):
+        out = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 300, 300, 128, causal=causal,
+                           window_size=(-1 if window is None else window, 0),
+                           tile_config=tile_config)
+        want = oracle_full(c, 1 / 128, causal=causal, window_left=window)
+        assert_close(np32(out), want)
+        assert torch.all(out[-5:] == 0)
+    ref = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 300, 300, 128, tile_config=1)
+    got = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 300, 300, 128,
+                       tile_config=tile_config)
+    # variants differ only in the last bits of some p values: at most one bf16 ulp of the output
+    assert_close(np32(got), np32(ref), atol=1e-2, rtol=1e-2)
+
+
+def test_window_row_without_keys_is_zero_in_default_config():
+    # bottom-right chunk shorter than a window gap: early query rows see no key at all
+    c = to_dev(make_case([64], [64], 4, 4, 64, seed=13))
+    out = run_prefill(c, causal_align="bottom_right", window_size=(0, 0))
+    want = oracle_full(c, 1 / 128, window_left=0, causal_align="bottom_right")
+    assert_close(np32(out), want)
