@@ -130,6 +130,28 @@ int ifa4_decode_launch(const IFA4DecodeParams* params, void* workspace, size_t w
 int ifa4_decode_workspace_size(const IFA4DecodeParams* params, size_t* bytes_out,
                                int32_t* num_splits_out, int32_t* chunk_len_out);
 
+/* Size of the library-owned decode scratch used by ifa4_decode_launch_noalloc (16 MiB). */
+#define IFA4_NOALLOC_DECODE_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* Decode for callers that cannot allocate device memory.  No counterpart in the reference.
+ *
+ * Some callers may not call cudaMalloc: a serving engine that reserves all device memory up
+ * front and forbids allocation on its request path, or a plugin reached through a C FFI that
+ * has no handle on its host's allocator and so cannot hand ifa4_decode_launch a workspace.
+ * This entry point takes no workspace and allocates nothing: the split-KV partials go to a
+ * statically sized array inside the library (IFA4_NOALLOC_DECODE_SCRATCH_BYTES), which every
+ * GPU that loads the library holds until the process exits.
+ *
+ * Same parameters and results as ifa4_decode_launch.  With num_splits = 0 the split count is
+ * capped so the partials fit the array; an explicit num_splits whose partials would not fit
+ * is rejected with IFA4_ERR_WORKSPACE.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  All calls share the one array: calls whose kernels overlap on
+ * the GPU (different streams, or different host threads) race on it, so serialise them.
+ * Nothing in the array needs to start at zero: every split writes its whole partial before
+ * the combine kernel reads it. */
+int ifa4_decode_launch_noalloc(const IFA4DecodeParams* params, void* stream);
+
 /* Reads (and optionally clears) the library's device status word on `stream`, blocking the
  * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on
  * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode.  Test hook; the

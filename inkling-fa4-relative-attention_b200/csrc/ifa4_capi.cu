@@ -353,6 +353,71 @@ int ifa4_decode_launch(const IFA4DecodeParams* p, void* workspace, size_t worksp
   return IFA4_OK;
 }
 
+// ---------------------------------------------------------------------------------------
+// Decode without allocation: for callers that may not call cudaMalloc (an engine that
+// reserved all device memory up front, or an FFI plugin with no access to its host's
+// allocator).  The split-KV partials live in this file-scope array instead of a caller
+// workspace; every GPU that loads the library holds it until the process exits.  In host code
+// the symbol is only a stand-in, so the device address is looked up once per device
+// (cudaGetSymbolAddress with that device current) and passed to the kernels.
+// ---------------------------------------------------------------------------------------
+}  // extern "C"
+
+static __device__ __align__(256) float g_ifa4_decode_scratch[IFA4_NOALLOC_DECODE_SCRATCH_BYTES /
+                                                              sizeof(float)];
+
+namespace {
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// First call on a device: resolves the scratch array's device address for the current device.
+int decode_scratch_ptr(void** out) {
+  int dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ifa4_decode_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return IFA4_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ifa4_decode_launch_noalloc(const IFA4DecodeParams* p, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = validate_common(p, "decode_noalloc");
+  if (rc) return rc;
+  if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
+  int splits, chunk;
+  size_t ws = 0;
+  if ((rc = decode_plan(p, &splits, &chunk, &ws))) return rc;
+  const size_t per_split = static_cast<size_t>(p->batch) * p->n_heads * (128 + 1) * sizeof(float);
+  if (ws > IFA4_NOALLOC_DECODE_SCRATCH_BYTES) {
+    if (p->num_splits != 0)
+      return fail(IFA4_ERR_WORKSPACE,
+                  "decode_noalloc: num_splits %d needs %zu bytes of scratch; the static scratch "
+                  "holds %u bytes (at most %zu splits for batch %d x %d heads)",
+                  p->num_splits, ws, IFA4_NOALLOC_DECODE_SCRATCH_BYTES,
+                  static_cast<size_t>(IFA4_NOALLOC_DECODE_SCRATCH_BYTES) / per_split, p->batch,
+                  p->n_heads);
+    // automatic plan: cap the split count so the partials fit (CTAs stride over the chunks)
+    size_t fit = static_cast<size_t>(IFA4_NOALLOC_DECODE_SCRATCH_BYTES) / per_split;
+    splits = fit >= 2 ? static_cast<int>(fit) : 1;
+  }
+  IFA4DecodeParams q = *p;
+  q.num_splits = splits;
+  q.chunk_len = chunk;
+  void* scratch = nullptr;
+  if (splits > 1 && (rc = decode_scratch_ptr(&scratch))) return rc;
+  return ifa4_decode_launch(&q, scratch, splits > 1 ? IFA4_NOALLOC_DECODE_SCRATCH_BYTES : 0,
+                            stream);
+}
+
 int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out) {
   g_last_error[0] = '\0';
   if (status_out == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "status_out is NULL");

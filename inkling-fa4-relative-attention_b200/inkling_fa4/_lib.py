@@ -20,10 +20,12 @@ IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0
 ABI_VERSION = 1
+NOALLOC_DECODE_SCRATCH_BYTES = 16 * 1024 * 1024
 
 EXPORTED_SYMBOLS = (
     "ifa4_prefill_launch",
     "ifa4_decode_launch",
+    "ifa4_decode_launch_noalloc",
     "ifa4_decode_workspace_size",
     "ifa4_read_device_status",
     "ifa4_prefill_tile_config_name",
@@ -88,6 +90,8 @@ def lib() -> ctypes.CDLL:
     L.ifa4_prefill_launch.restype = ctypes.c_int
     L.ifa4_decode_launch.argtypes = [ctypes.POINTER(DecodeParams), vp, sz, vp]
     L.ifa4_decode_launch.restype = ctypes.c_int
+    L.ifa4_decode_launch_noalloc.argtypes = [ctypes.POINTER(DecodeParams), vp]
+    L.ifa4_decode_launch_noalloc.restype = ctypes.c_int
     L.ifa4_decode_workspace_size.argtypes = [ctypes.POINTER(DecodeParams), ctypes.POINTER(sz),
                                              ctypes.POINTER(i32), ctypes.POINTER(i32)]
     L.ifa4_decode_workspace_size.restype = ctypes.c_int
