@@ -269,7 +269,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           pa[r] = pack_bf16x2(p00, p01);      // a0 (r=0) / a1 (r=1): keys 0..7 of the k16
           pa[2 + r] = pack_bf16x2(p10, p11);  // a2 / a3: keys 8..15
         }
-        // ---- O += P V  (V^T fragments via transposed ldmatrix)
+        // ---- O += P V  (V^T fragments via transposed ldmatrix).  The bias/mask code above
+        // branches per lane; ldmatrix/mma are .sync.aligned: reconverge the warp first.
+        __syncwarp();
         {
           const int mi = lane >> 3;
           const int vrow = wrow + (mi & 1) * 8 + (lane & 7);

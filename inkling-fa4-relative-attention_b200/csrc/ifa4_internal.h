@@ -33,11 +33,13 @@ struct PrefillLaunch {
   int smem_bytes;
 };
 
-// Prefill tile configurations: the kernel variants differ in how many of every 16 score
-// columns get their exponential from the FMA-pipe polynomial instead of the SFU.
-// tile_config 0 = default, 1..5 = 0, 2, 4, 6, 8 emulated columns of 16.
+// Prefill tile configurations: the kernel variants differ in where the exponentials of every 16
+// score columns are computed: FMA-pipe polynomial, SFU two-at-a-time (f16x2), or SFU fp32.
+// tile_config 0 = default; 1..5 = 0, 2, 4, 6, 8 polynomial columns of 16; 6 = all f16x2;
+// 7 = 8 of 16 f16x2; 8 = 4 polynomial + 8 f16x2.
 constexpr int kPrefillDefaultEmu = 0;
-constexpr int kPrefillNumTileConfigs = 6;
+constexpr int kPrefillDefaultHalf2 = 0;
+constexpr int kPrefillNumTileConfigs = 9;
 int prefill_emulated_exp_columns(int tile_config);  // -1 for an unknown id
 
 // Launches the tcgen05 prefill kernel variant of `tile_config`.  Returns a cudaError_t.

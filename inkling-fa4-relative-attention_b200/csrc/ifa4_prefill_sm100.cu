@@ -50,15 +50,6 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;                // log2 units: rescale O at 256x
 
-// Register split: warpgroup 0 (producer, MMA issuer, TMEM owner, spare) drops to kRegsCtl,
-// the two softmax warpgroups rise to kRegsSoftmax.  4*32*kRegsCtl + 8*32*kRegsSoftmax must not
-// exceed the 384 * kLaunchRegs registers the CTA is launched with, or setmaxnreg.inc would wait
-// forever; inkling_fa4/build.py fails the build unless ptxas reports exactly kLaunchRegs.
-constexpr int kLaunchRegs = 168;
-constexpr int kRegsCtl = 64;
-constexpr int kRegsSoftmax = 216;
-static_assert(4 * 32 * kRegsCtl + 8 * 32 * kRegsSoftmax <= kThreads * kLaunchRegs,
-              "register split exceeds the launch allocation");
 
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
@@ -142,7 +133,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint3
   }
 }
 
-template <int kEmu>
+template <int kEmu, int kHalf2>
 __global__ void __launch_bounds__(kThreads, 1)
     rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
                             const __grid_constant__ CUtensorMap tm_q,
@@ -167,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    mbar_init(&bars->q_empty, 1);
+    mbar_init(&bars->q_empty, 1 + 8);  // MMA commit + 8 softmax warps (epilogue staging)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
@@ -197,7 +188,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = bars->tmem_base;
   const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
   if (warp < 4) {
-   regs_dec<kRegsCtl>();
    if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -318,7 +308,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
    }
   } else {
-    regs_inc<kRegsSoftmax>();
     // ------------------------------------------------------------------ softmax
     const int s = (warp - 4) >> 2;
     const int row = (warp & 3) * 32 + lane;
@@ -357,17 +346,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait_warp(&bars->s_full[s], pc & 1, ab))) break;
         ++pc;
         tc_fence_after();
-        float x[128];
-        {
-          uint32_t r[4][32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[c][i]);
-        }
         const int k0 = (t.j_lo + j) * kBN;
         // relative bias: keys in [dmax - R + 1, dmax] carry rel[row, dmax - key]
         const int bl = dmax - a.rel_extent + 1 - k0;  // first column with bias
@@ -375,38 +353,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int cl = key_lo - k0, ch = key_hi - k0;  // visible columns [cl, ch)
         const bool has_bias = row_valid && bl <= 127 && bh >= 0;
         const bool has_mask = cl > 0 || ch < kBN;
-        // Interior rows keep raw scores (the scale is folded into the exponent FMA); rows with
-        // bias or mask turn x into the scaled, biased, masked logit first.
-        float mul = a.scale_log2;
-        if (has_bias || has_mask) {
+        // Pass 1 — the row max.  In a warp where no row needs bias or mask it is taken over the
+        // raw scores and the scale is folded into the exponent FMA (mul = scale*log2e).
+        // Otherwise every lane turns its scores into the scaled, biased, masked logit chunk by
+        // chunk and writes it back over S in TMEM, and pass 2 reads logits (mul = 1).
+        float mul, m_tile;
+        if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
+          uint32_t r[4][32];
 #pragma unroll
-          for (int c = 0; c < 128; ++c) x[c] *= a.scale_log2;
-          if (has_bias) {
+          for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
+          tmem_wait_ld();
+          float mA = __uint_as_float(r[0][0]), mB = __uint_as_float(r[0][1]);
+          float mC = __uint_as_float(r[0][2]), mD = __uint_as_float(r[0][3]);
 #pragma unroll
-            for (int c = 0; c < 128; ++c) {
-              if (c >= bl && c <= bh) {
-                const uint16_t bits = __ldg(rel_row + (bh - c));
-                x[c] += bf16_bits_to_float(bits) * kLog2e;
+          for (int c = 4; c < 128; c += 8) {
+            const uint32_t* v = &r[c >> 5][c & 31];
+            mA = fmax3(mA, __uint_as_float(v[0]), __uint_as_float(v[1]));
+            mB = fmax3(mB, __uint_as_float(v[2]), __uint_as_float(v[3]));
+            mC = fmax3(mC, __uint_as_float(v[4]), __uint_as_float(v[5]));
+            mD = fmax3(mD, __uint_as_float(v[6]), __uint_as_float(v[7]));
+          }
+          mul = a.scale_log2;
+          m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
+        } else {
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_s + c * 32, r);
+            tmem_wait_ld();
+            float x[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
+            if (has_bias) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int col = c * 32 + i;
+                if (col >= bl && col <= bh)
+                  x[i] += bf16_bits_to_float(__ldg(rel_row + (bh - col))) * kLog2e;
               }
             }
-          }
-          if (has_mask) {
+            if (has_mask) {
 #pragma unroll
-            for (int c = 0; c < 128; ++c)
-              if (c < cl || c >= ch) x[c] = -INFINITY;
+              for (int i = 0; i < 32; ++i) {
+                const int col = c * 32 + i;
+                if (col < cl || col >= ch) x[i] = -INFINITY;
+              }
+            }
+            float m0 = x[0], m1 = x[1];
+#pragma unroll
+            for (int i = 2; i < 32; i += 4) {
+              m0 = fmax3(m0, x[i], x[i + 1]);
+              m1 = fmax3(m1, x[i + 2], x[i + 3]);
+            }
+            mx = fmax3(mx, m0, m1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
+            __syncwarp();  // reconverge after the per-row branches: tcgen05.st is .aligned
+            tmem_st32(t_s + c * 32, r);
           }
+          tmem_wait_st();  // pass 2 reads these columns back
           mul = 1.f;
+          m_tile = mx;
         }
-        // row max: four independent chains of 3-input max
-        float mA = x[0], mB = x[1], mC = x[2], mD = x[3];
-#pragma unroll
-        for (int c = 4; c < 128; c += 8) {
-          mA = fmax3(mA, x[c], x[c + 1]);
-          mB = fmax3(mB, x[c + 2], x[c + 3]);
-          mC = fmax3(mC, x[c + 4], x[c + 5]);
-          mD = fmax3(mD, x[c + 6], x[c + 7]);
-        }
-        const float m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
         const float m_new = fmaxf(m_run, m_tile);
         float alpha = 1.f;
         bool need_rescale = false;
@@ -419,21 +428,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_run = m_new;
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        // p = 2^(x * mul - m_use): kEmu of every 16 columns on the FMA pipe, the rest on the SFU
+        __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
+        // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks, loading chunk c+1 while
+        // chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
+        // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
+        // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
         const uint64_t mul2 = f2_pack(mul, mul);
         const uint64_t neg2 = f2_pack(-m_use, -m_use);
         uint64_t acc[4] = {0, 0, 0, 0};
+        uint32_t rr[2][32];
+        tmem_ld32(t_s, rr[0]);
+        tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
+          if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int col = c * 32 + 2 * i;
             float y0, y1;
-            f2_unpack(f2_fma(f2_pack(x[col], x[col + 1]), mul2, neg2), y0, y1);
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[c & 1][2 * i]),
+                                     __uint_as_float(rr[c & 1][2 * i + 1])),
+                             mul2, neg2),
+                      y0, y1);
             float p0, p1;
             if ((col & 15) < kEmu) {
               exp2_poly_pair(y0, y1, p0, p1);
+            } else if ((col & 15) < kEmu + kHalf2) {
+              exp2_h2_pair(y0, y1, p0, p1);
             } else {
               p0 = fast_exp2(y0);
               p1 = fast_exp2(y1);
@@ -442,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             pk[i] = pack_bf16x2(p0, p1);
           }
           tmem_st16(t_s + c * 16, pk);
+          if (c < 3) tmem_wait_ld();
         }
         {
           const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
@@ -462,37 +485,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(t_o + c * 32, o);
           }
         }
+        __syncwarp();
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->p_full[s]);
       }
       if (!ok) break;
-      // epilogue
+      // epilogue: O / l -> bf16, staged through this sub-tile's Q buffer (idle once O is final:
+      // every MMA reading Q completed before the last PV) with the 128-B swizzle, then written
+      // back by the warp as whole 256-byte rows (coalesced).  The producer reloads Q only after
+      // the MMA commit and all 8 softmax warps have arrived on q_empty.
       if (!(ok = mbar_wait_warp(&bars->o_full[s], oc & 1, ab))) break;
       ++oc;
       tc_fence_after();
       // a row that never saw a visible key outputs 0 (the FMA-pipe exp2 of a masked
       // logit is ~2^-125, not 0, so l alone does not tell)
       const float inv_l = (l_run > 0.f && m_run != -INFINITY) ? 1.f / l_run : 0.f;
+      uint8_t* stage = smem + kSmemQ + s * kTile;
+      __syncwarp();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         tmem_ld32(t_o + c * 32, o);
         tmem_wait_ld();
-        if (row_valid) {
-          uint32_t pk[16];
+        if (c == 3) {
+          tc_fence_before();
+          mbar_arrive(&bars->o_empty[s]);  // TMEM O may be overwritten by the next work tile
+        }
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
-                                __uint_as_float(o[2 * i + 1]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(out_row + c * 32);
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
+                              __uint_as_float(o[2 * i + 1]) * inv_l);
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        for (int v = 0; v < 4; ++v) {
+          const int g = c * 4 + v;  // 16-byte granule of the 256-byte row
+          uint4* dst = reinterpret_cast<uint4*>(stage + (g >> 3) * kHalf + row * 128 +
+                                                (((g & 7) ^ (row & 7)) << 4));
+          *dst = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&bars->o_empty[s]);
+      __syncwarp();
+      {
+        const int wrow0 = (warp & 3) * 32;
+        const int g = lane & 15;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int r = wrow0 + 2 * i + (lane >> 4);
+          const uint4 val = *reinterpret_cast<const uint4*>(
+              stage + (g >> 3) * kHalf + r * 128 + (((g & 7) ^ (r & 7)) << 4));
+          const int qr = t.row0[s] + r;
+          if (qr < sq) {
+            uint16_t* dst = a.out + static_cast<long long>(q_start + qr) * a.out_st +
+                            static_cast<long long>(h) * a.out_sh + g * 8;
+            *reinterpret_cast<uint4*>(dst) = val;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->q_empty);
     }
   }
 
@@ -507,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace prefill
 
 namespace {
-template <int kEmu>
+template <int kEmu, int kHalf2>
 cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
                            cudaStream_t stream) {
@@ -518,28 +569,26 @@ cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu>,
+    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu, kHalf2>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(prefill::kSmemAlloc));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  prefill::rel_attn_prefill_kernel<kEmu>
+  prefill::rel_attn_prefill_kernel<kEmu, kHalf2>
       <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
   return cudaGetLastError();
 }
 }  // namespace
 
+// tile_config -> (columns of 16 on the FMA-pipe polynomial, columns of 16 on SFU f16x2)
+static const int kVariants[kPrefillNumTileConfigs][2] = {
+    {kPrefillDefaultEmu, kPrefillDefaultHalf2}, {0, 0}, {2, 0}, {4, 0}, {6, 0}, {8, 0},
+    {0, 16}, {0, 8}, {4, 8}};
+
 int prefill_emulated_exp_columns(int tile_config) {
-  switch (tile_config) {
-    case 0: return kPrefillDefaultEmu;
-    case 1: return 0;
-    case 2: return 2;
-    case 3: return 4;
-    case 4: return 6;
-    case 5: return 8;
-    default: return -1;
-  }
+  if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return -1;
+  return kVariants[tile_config][0];
 }
 
 cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
@@ -547,14 +596,20 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
                                  int q_slots, int tile_config, cudaStream_t stream) {
   const int head_slots = args.pair_heads ? args.n_heads / 2 : args.n_heads;
   dim3 grid(head_slots, args.batch, q_slots);
-  switch (prefill_emulated_exp_columns(tile_config)) {
-    case 0: return launch_variant<0>(args, tm_q, tm_k, tm_v, grid, stream);
-    case 2: return launch_variant<2>(args, tm_q, tm_k, tm_v, grid, stream);
-    case 4: return launch_variant<4>(args, tm_q, tm_k, tm_v, grid, stream);
-    case 6: return launch_variant<6>(args, tm_q, tm_k, tm_v, grid, stream);
-    case 8: return launch_variant<8>(args, tm_q, tm_k, tm_v, grid, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return cudaErrorInvalidValue;
+  const int emu = kVariants[tile_config][0], h2 = kVariants[tile_config][1];
+#define IFA4_VARIANT(E, H) \
+  if (emu == E && h2 == H) return launch_variant<E, H>(args, tm_q, tm_k, tm_v, grid, stream);
+  IFA4_VARIANT(0, 0)
+  IFA4_VARIANT(2, 0)
+  IFA4_VARIANT(4, 0)
+  IFA4_VARIANT(6, 0)
+  IFA4_VARIANT(8, 0)
+  IFA4_VARIANT(0, 16)
+  IFA4_VARIANT(0, 8)
+  IFA4_VARIANT(4, 8)
+#undef IFA4_VARIANT
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace ifa4

@@ -188,17 +188,6 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                : "memory");
 }
 
-// Warpgroup register re-balancing (all 128 threads of the warpgroup execute it).  The sum of the
-// warpgroups' new counts must not exceed what the CTA was launched with, or `inc` never returns.
-template <int kRegs>
-__device__ __forceinline__ void regs_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-template <int kRegs>
-__device__ __forceinline__ void regs_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -390,6 +379,20 @@ __device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, fl
   f2_unpack(t, t0, t1);
   y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
   y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// 2^x for a pair of floats with one SFU instruction (ex2.approx.f16x2): the inputs are rounded
+// to fp16 (10-bit mantissa; the arguments are <= 8 here, so the input rounding changes the
+// result by at most 0.14 %, below the bf16 rounding applied to it next) and the fp16 results
+// are widened back.  Inputs below -25 give 0 or an fp16 subnormal (< 2^-24).
+__device__ __forceinline__ void exp2_h2_pair(float x0, float x1, float& y0, float& y1) {
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(y0), "=f"(y1)
+      : "r"(e));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

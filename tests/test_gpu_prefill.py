@@ -152,7 +152,7 @@ def test_config_chunked_spot_rows():
     assert_close(got, want)
 
 
-@pytest.mark.parametrize("tile_config", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("tile_config", [1, 2, 3, 4, 5, 6, 7, 8])
 def test_tile_config_variants_match_oracle(tile_config):
     """Every kernel variant (fraction of exponentials computed on the FMA pipe) is correct,
     including rows that see no key (must be 0, not the ~2^-125 of an emulated exp2(-inf))."""
