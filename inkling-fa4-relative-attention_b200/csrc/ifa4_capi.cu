@@ -229,7 +229,8 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   if (slots < 1) slots = 1;
   if (slots > 65535) slots = 65535;
   cudaError_t e = ifa4::launch_prefill_sm100(a, tq, tk, tv, static_cast<int>(slots),
-                                             p->tile_config, static_cast<cudaStream_t>(stream));
+                                             p->tile_config, static_cast<int>(max_sq),
+                                             static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return IFA4_OK;
 }

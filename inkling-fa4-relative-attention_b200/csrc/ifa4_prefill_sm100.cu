@@ -44,7 +44,13 @@ constexpr uint32_t kSmemQ = 0;                           // 2 sub-tiles
 constexpr uint32_t kSmemK = 2 * kTile;                   // 2 stages
 constexpr uint32_t kSmemV = 4 * kTile;                   // 2 stages
 constexpr uint32_t kSmemBar = 6 * kTile;                 // barriers + slots
-constexpr uint32_t kSmemBytes = kSmemBar + 256;
+// Per softmax warp, a 32-row x 32-column bf16 transpose buffer for the relative-bias gather;
+// rows are 34 halfwords (17 words) apart so both the row writes and the per-lane row reads are
+// free of bank conflicts.
+constexpr uint32_t kBiasRowHalves = 34;
+constexpr uint32_t kBiasWarpBytes = 32 * kBiasRowHalves * 2;
+constexpr uint32_t kSmemBias = kSmemBar + 256;
+constexpr uint32_t kSmemBytes = kSmemBias + 8 * kBiasWarpBytes;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // slack for 1024-B alignment
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -165,9 +171,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], kBM);
+      mbar_init(&bars->p_full[i], 4);   // one arrival per softmax warp
       mbar_init(&bars->o_full[i], 1);
-      mbar_init(&bars->o_empty[i], kBM);
+      mbar_init(&bars->o_empty[i], 4);
     }
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
@@ -340,6 +346,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (a.causal) key_hi = min(key_hi, qi + ms + 1);
       const int key_lo = a.window_left >= 0 ? max(0, qi + ms - a.window_left) : 0;
       const int dmax = qi + bs;  // bias distance at key 0
+      // The band tiles (those whose distances meet [0, R)) come last in the KV loop; start
+      // pulling this row's bias into L2 now so their gather finds it there.
+      if (row_valid) {  // addresses stay inside the row's R elements
+        const int n = min((a.rel_extent + 63) / 64, 16);
+        for (int i = 0; i < n; ++i) prefetch_l2(rel_row + i * 64);
+      }
+      uint16_t* bias_buf = reinterpret_cast<uint16_t*>(smem + kSmemBias + (warp - 4) * kBiasWarpBytes);
       float m_run = -INFINITY, l_run = 0.f;
 
       for (int j = 0; j < t.n_kv; ++j) {
@@ -385,13 +398,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             float x[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
-            if (has_bias) {
+            // Relative bias, gathered by the whole warp: for each of the warp's 32 rows the
+            // lanes load that row's 32 consecutive values (one coalesced 64-byte access),
+            // store them to the transpose buffer, and each lane then reads its own row.
+            // Columns outside [bl, bh] (or rows without bias) read 0.
+            const bool chunk_bias = has_bias && c * 32 + 31 >= bl && c * 32 <= bh;
+            if (__any_sync(0xffffffffu, chunk_bias)) {
+              uint16_t* buf = bias_buf;
+              const int col = c * 32 + lane;
+              uint16_t v[32];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int col = c * 32 + i;
-                if (col >= bl && col <= bh)
-                  x[i] += bf16_bits_to_float(__ldg(rel_row + (bh - col))) * kLog2e;
+              for (int tr = 0; tr < 32; ++tr) {  // all 32 loads in flight before any use
+                const int qi_t = qi - lane + tr;  // row of lane tr in this warp
+                const int d = qi_t + bs - k0 - col;
+                v[tr] = 0;
+                if (qi_t < sq && d >= 0 && d < a.rel_extent)
+                  v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
               }
+#pragma unroll
+              for (int tr = 0; tr < 32; ++tr) buf[tr * kBiasRowHalves + lane] = v[tr];
+              __syncwarp();
+              const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + lane * (kBiasRowHalves / 2);
+#pragma unroll
+              for (int k = 0; k < 16; ++k) {
+                const uint32_t pr = w[k];
+                x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
+                x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
+              }
+              __syncwarp();
             }
             if (has_mask) {
 #pragma unroll
@@ -485,10 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(t_o + c * 32, o);
           }
         }
-        __syncwarp();
+        // every lane's TMEM stores are complete and fenced before lane 0 releases P
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&bars->p_full[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[s]);
       }
       if (!ok) break;
       // epilogue: O / l -> bf16, staged through this sub-tile's Q buffer (idle once O is final:
@@ -508,9 +543,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t o[32];
         tmem_ld32(t_o + c * 32, o);
         tmem_wait_ld();
-        if (c == 3) {
+        if (c == 3) {  // TMEM O may be overwritten by the next work tile
           tc_fence_before();
-          mbar_arrive(&bars->o_empty[s]);  // TMEM O may be overwritten by the next work tile
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->o_empty[s]);
         }
         uint32_t pk[16];
 #pragma unroll
@@ -593,11 +629,20 @@ int prefill_emulated_exp_columns(int tile_config) {
 
 cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                                 int q_slots, int tile_config, cudaStream_t stream) {
+                                 int q_slots, int tile_config, int max_seqlen_q,
+                                 cudaStream_t stream) {
   const int head_slots = args.pair_heads ? args.n_heads / 2 : args.n_heads;
   dim3 grid(head_slots, args.batch, q_slots);
   if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return cudaErrorInvalidValue;
-  const int emu = kVariants[tile_config][0], h2 = kVariants[tile_config][1];
+  int emu = kVariants[tile_config][0], h2 = kVariants[tile_config][1];
+  if (tile_config == 0) {
+    // Measured on B200 (interleaved A/B, GQA 32/8): on long causal sequences the SFU is the
+    // softmax bottleneck and 4 of 16 exponentials on the FMA pipe win (32k: 975 vs 921
+    // TFLOP/s); with a 4096 window (boundary tiles dominate) or on short ragged sequences
+    // (<= 4k: 425 vs 458) the all-SFU variant wins.
+    emu = (args.window_left < 0 && max_seqlen_q >= 16384) ? 4 : 0;
+    h2 = 0;
+  }
 #define IFA4_VARIANT(E, H) \
   if (emu == E && h2 == H) return launch_variant<E, H>(args, tm_q, tm_k, tm_v, grid, stream);
   IFA4_VARIANT(0, 0)

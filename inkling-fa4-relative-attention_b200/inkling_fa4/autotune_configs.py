@@ -29,13 +29,20 @@ PRESETS = {
 # bench.py --only prefill (32k causal, GQA 32/8): TFLOP/s per variant.  tile_config 0 resolves
 # to the fastest.
 TILE_CONFIGS = {
-    0: {"emulated_exp_of_16": 0, "note": "default (= tile_config 1)"},
-    1: {"emulated_exp_of_16": 0, "causal32k_tflops": 1019.5},
-    2: {"emulated_exp_of_16": 2, "causal32k_tflops": 902.8},
-    3: {"emulated_exp_of_16": 4, "causal32k_tflops": 882.0},
-    4: {"emulated_exp_of_16": 6, "causal32k_tflops": 869.9},
-    5: {"emulated_exp_of_16": 8, "causal32k_tflops": 865.9},
+    0: {"note": "automatic: tile_config 3 for max_seqlen_q >= 16384 without a window, else 1"},
+    1: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 0},
+    2: {"emulated_exp_of_16": 2, "sfu_f16x2_of_16": 0},
+    3: {"emulated_exp_of_16": 4, "sfu_f16x2_of_16": 0},
+    4: {"emulated_exp_of_16": 6, "sfu_f16x2_of_16": 0},
+    5: {"emulated_exp_of_16": 8, "sfu_f16x2_of_16": 0},
+    6: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 16},
+    7: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 8},
+    8: {"emulated_exp_of_16": 4, "sfu_f16x2_of_16": 8},
 }
+# Interleaved A/B on one B200 (7 rounds x 5 calls, medians), 32k GQA 32/8, TFLOP/s:
+#   causal:      tc1 920.8  tc3 974.7  tc6 873.3  tc7 934.8  tc8 936.0
+#   window 4096: tc1 776.2  tc3 759.0  tc6 710.3  tc7 762.5  tc8 740.5
+# ragged (config 2, <= 4k tokens): all-SFU 458 vs tc3 425.
 DECODE_PRESET = {"BLOCK_K": 64, "num_warps": 5, "num_stages": 3, "chunk_len": 0, "num_splits": 0}
 
 
