@@ -346,7 +346,8 @@ def main():
                      "peak_source": f"bf16_tflops (burst) of {peak_kind}",
                      "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                      "frac_of_datasheet_2250": achieved / 2250.0,
-                     "traffic": profile_traffic("prefill_causal32k_ncu.txt") if S == SEQ else None,
+                     "traffic": profile_traffic("prefill_dram_traffic.md") if S == SEQ else None,
+                     "traffic_note": "8k capture scaled x4 (profiles/prefill_dram_traffic.md)",
                      "kernel": "rel_attn_prefill_kernel (1 launch per step)",
                      "tile_config": args.tile_config},
         "gpu_launches": args.steps,
@@ -494,7 +495,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": per_gpu / peaks["hbm_gbs"],
                          "peak_source": f"hbm_gbs of {peak_kind}",
-                         "traffic": (profile_traffic("decode_b128_ncu.txt")
+                         "traffic": (profile_traffic("decode_dram_traffic.md")
                                      if args.decode_batch == 128 else None)},
             "gpu_launches": args.steps * (2 if nsplit > 1 else 1)}
         del dc, ws
