@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define IFA4_ABI_VERSION 1
+#define IFA4_ABI_VERSION 2
 
 enum {
   IFA4_OK = 0,
@@ -75,6 +75,11 @@ typedef struct IFA4PrefillParams {
   int32_t dtype;            /* IFA4_DTYPE_BF16                                         */
   float softmax_scale;      /* > 0; the reference uses 1/head_dim                      */
   int32_t tile_config;      /* 0 = automatic; see ifa4_prefill_tile_config_name        */
+  /* Optional fp32 log-sum-exp of each row's scaled+biased logits (natural log; -inf for a
+   * row with no visible key), written at lse[h * lse_stride_h + token * lse_stride_t] when
+   * lse != NULL.  Not in the reference; callers merge split attention with it. */
+  float* lse;
+  int64_t lse_stride_h, lse_stride_t;
 } IFA4PrefillParams;
 
 /* Prefill.  Replaces the per-sequence launch loop of inkling_fa4_rel_attention_triton
@@ -115,6 +120,8 @@ typedef struct IFA4DecodeParams {
   float softmax_scale;
   int32_t num_splits;       /* 0 = automatic (from max_seqlen_k and the SM count)      */
   int32_t chunk_len;        /* 0 = automatic; otherwise a multiple of 64               */
+  float* lse;               /* optional, as in IFA4PrefillParams (token = the query row) */
+  int64_t lse_stride_h, lse_stride_t;
 } IFA4DecodeParams;
 
 /* Decode.  Replaces inkling_fa4_rel_attention_decode_triton

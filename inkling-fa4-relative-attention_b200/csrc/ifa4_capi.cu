@@ -209,6 +209,9 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   const int group = p->n_heads / p->kv_heads;
   a.pair_heads = (group % 2 == 0) ? 1 : 0;
   a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  a.lse = p->lse;
+  a.lse_sh = p->lse_stride_h;
+  a.lse_st = p->lse_stride_t;
   a.status = status;
 
   CUtensorMap tq, tk, tv;
@@ -340,6 +343,9 @@ int ifa4_decode_launch(const IFA4DecodeParams* p, void* workspace, size_t worksp
     a.ws_o = static_cast<float*>(workspace);
     a.ws_lse = a.ws_o + parts * 128;
   }
+  a.lse = p->lse;
+  a.lse_sh = p->lse_stride_h;
+  a.lse_st = p->lse_stride_t;
   a.status = status;
   CUtensorMap tk, tv;
   const int64_t krows = p->total_k > 0 ? p->total_k : 1;

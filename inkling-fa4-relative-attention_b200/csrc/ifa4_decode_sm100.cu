@@ -339,6 +339,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                         static_cast<long long>(h) * a.out_sh + d;
         __nv_bfloat16 bv = __float2bfloat16_rn(val);
         *dst = *reinterpret_cast<uint16_t*>(&bv);
+        if (d == 0 && a.lse != nullptr)
+          a.lse[static_cast<long long>(h) * a.lse_sh + static_cast<long long>(si.q_row) * a.lse_st] =
+              L > 0.f ? (M + __log2f(L)) * 0.6931471805599453f : -INFINITY;
       } else {
         const long long idx = (static_cast<long long>(b) * a.n_heads + h) * gridDim.x + split;
         a.ws_o[idx * 128 + d] = val;
@@ -366,6 +369,9 @@ __global__ void __launch_bounds__(128)
   }
   const float val = wsum > 0.f ? acc / wsum : 0.f;
   const int q_row = a.cu_q[b];
+  if (d == 0 && a.lse != nullptr)  // log2-sum-exp of the partials -> natural log
+    a.lse[static_cast<long long>(h) * a.lse_sh + static_cast<long long>(q_row) * a.lse_st] =
+        wsum > 0.f ? (M + __log2f(wsum)) * 0.6931471805599453f : -INFINITY;
   __nv_bfloat16 bv = __float2bfloat16_rn(val);
   a.out[static_cast<long long>(q_row) * a.out_st + static_cast<long long>(h) * a.out_sh + d] =
       *reinterpret_cast<uint16_t*>(&bv);

@@ -25,6 +25,8 @@ struct PrefillKernelArgs {
   int pair_heads;            // 1: the CTA's two sub-tiles are two heads at the same rows
                              // 0: the CTA's two sub-tiles are consecutive 128-row blocks
   float scale_log2;          // softmax_scale * log2(e)
+  float* lse;                // optional natural-log LSE, [h * lse_sh + token * lse_st]
+  long long lse_sh, lse_st;
   int* status;
 };
 
@@ -67,6 +69,8 @@ struct DecodeKernelArgs {
   float scale_log2;
   float* ws_o;               // [batch, n_heads, num_splits, 128] (num_splits > 1)
   float* ws_lse;             // [batch, n_heads, num_splits]      (num_splits > 1)
+  float* lse;                // optional natural-log LSE output
+  long long lse_sh, lse_st;
   int* status;
 };
 

@@ -336,6 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
           for (int c = 0; c < 16; ++c) reinterpret_cast<uint4*>(out_row)[c] = z;
+          if (a.lse != nullptr)
+            a.lse[static_cast<long long>(h) * a.lse_sh +
+                  static_cast<long long>(q_start + qi) * a.lse_st] = -INFINITY;
         }
         continue;
       }
@@ -535,7 +538,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       // a row that never saw a visible key outputs 0 (the FMA-pipe exp2 of a masked
       // logit is ~2^-125, not 0, so l alone does not tell)
-      const float inv_l = (l_run > 0.f && m_run != -INFINITY) ? 1.f / l_run : 0.f;
+      const bool seen = l_run > 0.f && m_run != -INFINITY;
+      const float inv_l = seen ? 1.f / l_run : 0.f;
+      if (a.lse != nullptr && row_valid)  // ln(sum exp) = ln2 * (m + log2 l) in the exp2 domain
+        a.lse[static_cast<long long>(h) * a.lse_sh + static_cast<long long>(q_start + qi) * a.lse_st] =
+            seen ? (m_run + __log2f(l_run)) * 0.6931471805599453f : -INFINITY;
       uint8_t* stage = smem + kSmemQ + s * kTile;
       __syncwarp();
 #pragma unroll

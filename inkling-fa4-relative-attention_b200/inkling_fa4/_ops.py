@@ -65,6 +65,24 @@ def _check_inputs(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, n_heads, kv
     return n_heads, kv_heads, rel_extent, window_left
 
 
+def _lse_buffer(q, n_heads, return_lse, lse):
+    """fp32 [n_heads, total_q] log-sum-exp output (flash-attention's varlen layout)."""
+    if lse is None and not return_lse:
+        return None
+    if lse is None:
+        lse = torch.empty((n_heads, q.shape[0]), dtype=torch.float32, device=q.device)
+    if lse.dtype != torch.float32 or lse.shape != (n_heads, q.shape[0]) or lse.device != q.device:
+        raise ValueError("lse must be a float32 [n_heads, total_q] tensor on q's device")
+    return lse
+
+
+def _fill_lse(p, lse):
+    if lse is None:
+        p.lse, p.lse_stride_h, p.lse_stride_t = None, 0, 0
+    else:
+        p.lse, p.lse_stride_h, p.lse_stride_t = lse.data_ptr(), lse.stride(0), lse.stride(1)
+
+
 def _fill_common(p, q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
                  window_left, causal_align):
     p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
@@ -109,11 +127,13 @@ def _prepare(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, causal, window_s
 def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
             rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
             head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
-            tile_config=0):
+            tile_config=0, return_lse=False, lse=None):
     q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
         "prefill", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
         window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out)
+    lse = _lse_buffer(q, n_heads, return_lse, lse)
     p = _lib.PrefillParams()
+    _fill_lse(p, lse)
     _fill_common(p, q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
                  rel_extent, causal, window_left, causal_align)
     p.max_seqlen_q = int(max_seqlen_q) if max_seqlen_q else 0
@@ -122,7 +142,7 @@ def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_s
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         _lib.check(_lib.lib().ifa4_prefill_launch(ctypes.byref(p), ctypes.c_void_p(stream)))
-    return out
+    return (out, lse) if lse is not None else out
 
 
 def _decode_params(q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
@@ -134,6 +154,7 @@ def _decode_params(q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent,
     p.softmax_scale = scale
     p.num_splits = int(num_splits)
     p.chunk_len = int(chunk_len)
+    _fill_lse(p, None)
     return p
 
 
@@ -150,10 +171,11 @@ def decode_plan(p) -> tuple[int, int, int]:
 def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
            rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
            head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
-           num_splits=0, chunk_len=0, workspace=None):
+           num_splits=0, chunk_len=0, workspace=None, return_lse=False, lse=None):
     q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
         "decode", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
         window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out)
+    lse = _lse_buffer(q, n_heads, return_lse, lse)
     if q.shape[0] != cu_seqlens_q.numel() - 1:
         raise ValueError("decode: expects exactly one query token per sequence")
     if q.stride(0) % 2 or q.stride(1) % 2:
@@ -161,6 +183,7 @@ def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_se
     p = _decode_params(q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
                        rel_extent, causal, window_left, causal_align, max_seqlen_k, scale,
                        num_splits, chunk_len)
+    _fill_lse(p, lse)
     with torch.cuda.device(q.device):
         nbytes, _, _ = decode_plan(p)
         if nbytes > 0 and (workspace is None or workspace.numel() * workspace.element_size() < nbytes):
@@ -170,4 +193,4 @@ def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_se
         stream = torch.cuda.current_stream(q.device).cuda_stream
         _lib.check(_lib.lib().ifa4_decode_launch(ctypes.byref(p), ctypes.c_void_p(ws_ptr),
                                                  ctypes.c_size_t(ws_len), ctypes.c_void_p(stream)))
-    return out
+    return (out, lse) if lse is not None else out

@@ -14,7 +14,8 @@ def inkling_fa4_rel_attention_triton(q, k, v, rel_logits, cu_seqlens_q, cu_seqle
                                      causal=True, window_size=(-1, -1),
                                      n_heads=None, kv_heads=None, head_dim=128,
                                      arch=None, *, softmax_scale=None,
-                                     causal_align="reference", out=None):
+                                     causal_align="reference", out=None, return_lse=False,
+                                     lse=None):
     """Relative-position-bias flash attention over packed variable-length sequences.
 
     Same arguments and meaning as the reference (triton_kernel.py:84-106):
@@ -30,12 +31,16 @@ def inkling_fa4_rel_attention_triton(q, k, v, rel_logits, cu_seqlens_q, cu_seqle
     local positions and bias offset sq - sk, reference.py:28-37; "bottom_right": both offset by
     sk - sq, the flash-attention convention for chunked prefill and decode), ``out``.
 
-    Returns ``out`` [total_q, n_heads, 128] bf16.  Rows with no visible key are 0.
+    Returns ``out`` [total_q, n_heads, 128] bf16.  Rows with no visible key are 0.  With
+    ``return_lse=True`` (or an ``lse`` buffer) also returns the fp32 natural-log log-sum-exp of
+    each row's scaled+biased logits, [n_heads, total_q] (-inf for rows with no visible key), for
+    merging attention computed over separate key ranges.
     """
     return _ops.prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
                         max_seqlen_k, rel_extent, causal=causal, window_size=window_size,
                         n_heads=n_heads, kv_heads=kv_heads, head_dim=head_dim,
-                        softmax_scale=softmax_scale, causal_align=causal_align, out=out)
+                        softmax_scale=softmax_scale, causal_align=causal_align, out=out,
+                        return_lse=return_lse, lse=lse)
 
 
 __all__ = ["inkling_fa4_rel_attention_triton"]

@@ -16,7 +16,8 @@ def inkling_fa4_rel_attention_decode_triton(q, k, v, rel_logits, cu_seqlens_q, c
                                             n_heads=None, kv_heads=None, head_dim=128,
                                             arch=None, *, softmax_scale=None,
                                             causal_align="reference", out=None,
-                                            num_splits=0, chunk_len=0, workspace=None):
+                                            num_splits=0, chunk_len=0, workspace=None,
+                                            return_lse=False, lse=None):
     """Decode: q [batch, n_heads, 128] (one query per sequence, cu_seqlens_q = 0..batch),
     k/v [total_k, kv_heads, 128], rel_logits [batch, n_heads, >=rel_extent].
 
@@ -25,13 +26,15 @@ def inkling_fa4_rel_attention_decode_triton(q, k, v, rel_logits, cu_seqlens_q, c
     ``softmax_scale``, ``causal_align`` (use "bottom_right" for the usual decode semantics in
     which the query is the last position of its sequence; "reference" reproduces the oracle,
     whose query sees key 0 only), ``out``, ``num_splits``/``chunk_len`` (0 = automatic) and a
-    reusable ``workspace`` (uint8 CUDA tensor; allocated per call when absent).
+    reusable ``workspace`` (uint8 CUDA tensor; allocated per call when absent), and
+    ``return_lse`` / ``lse`` as in the prefill entry point.
     """
     return _ops.decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
                        max_seqlen_k, rel_extent, causal=causal, window_size=window_size,
                        n_heads=n_heads, kv_heads=kv_heads, head_dim=head_dim,
                        softmax_scale=softmax_scale, causal_align=causal_align, out=out,
-                       num_splits=num_splits, chunk_len=chunk_len, workspace=workspace)
+                       num_splits=num_splits, chunk_len=chunk_len, workspace=workspace,
+                       return_lse=return_lse, lse=lse)
 
 
 __all__ = ["inkling_fa4_rel_attention_decode_triton"]

@@ -84,7 +84,7 @@ def alignment_offsets(sq: int, sk: int, causal_align: str) -> tuple[int, int]:
 
 
 def rel_attn_rows(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_extent,
-                  causal=True, window_left=None, causal_align="reference"):
+                  causal=True, window_left=None, causal_align="reference", return_lse=False):
     """Attention for a block of query rows of one (sequence, head).
 
     ``q_rows`` [n, d], ``k_b``/``v_b`` [sk, d], ``rel_rows`` [n, >=rel_extent] (float32),
@@ -92,7 +92,8 @@ def rel_attn_rows(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_extent,
     Follows reference.py:27-39 row by row.
     """
     if sk == 0:  # softmax over an empty key axis: the reference's einsum yields zeros
-        return np.zeros((q_rows.shape[0], v_b.shape[1]), dtype=np.float32)
+        z = np.zeros((q_rows.shape[0], v_b.shape[1]), dtype=np.float32)
+        return (z, np.full(q_rows.shape[0], -np.inf, np.float32)) if return_lse else z
     mask_shift, bias_shift = alignment_offsets(sq, sk, causal_align)
     scores = (q_rows @ k_b.T) * np.float32(scale)                       # reference.py:27
     qp = q_pos.reshape(-1, 1).astype(np.int64)
@@ -108,16 +109,20 @@ def rel_attn_rows(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_extent,
     if window_left is not None:                                          # reference.py:37
         scores = np.where((qp + mask_shift - kp) <= window_left, scores, -np.inf)
     scores = scores.astype(np.float32)
-    with np.errstate(invalid="ignore", over="ignore"):
+    with np.errstate(invalid="ignore", over="ignore", divide="ignore"):
         m = np.max(scores, axis=1, keepdims=True)                        # reference.py:38
         e = np.exp(scores - m)
-        p = e / np.sum(e, axis=1, keepdims=True)
-    return (p.astype(np.float32) @ v_b).astype(np.float32)              # reference.py:39
+        ssum = np.sum(e, axis=1, keepdims=True)
+        p = e / ssum
+        # log-sum-exp of the same logits (an extension for LSE checks; -inf if all masked)
+        lse = np.where(np.isfinite(m[:, 0]), m[:, 0] + np.log(ssum[:, 0]), -np.inf)
+    o = (p.astype(np.float32) @ v_b).astype(np.float32)                 # reference.py:39
+    return (o, lse.astype(np.float32)) if return_lse else o
 
 
 def rel_attn(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, scale, rel_extent,
              causal=True, window_left=None, causal_align="reference", row_block=None,
-             heads=None, out_bf16=False):
+             heads=None, out_bf16=False, return_lse=False):
     """numpy restatement of ``ref_rel_attn`` (reference.py:4-39).
 
     Args mirror the reference: q [Tq, Hq, d], k/v [Tk, Hkv, d], rel_logits [Tq, Hq, >=R]
@@ -136,6 +141,7 @@ def rel_attn(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, scale, rel_extent,
     n_heads, kv_heads = q.shape[1], k.shape[1]
     g = n_heads // kv_heads
     out = np.zeros(q.shape, dtype=np.float32)
+    lse_all = np.full((n_heads, q.shape[0]), -np.inf, dtype=np.float32)
     head_list = range(n_heads) if heads is None else heads
     for b in range(len(cu_q) - 1):                                       # reference.py:21
         qs, qe = int(cu_q[b]), int(cu_q[b + 1])
@@ -150,13 +156,15 @@ def rel_attn(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, scale, rel_extent,
             v_b = np.ascontiguousarray(v[ks:ke, kh])
             for r0 in range(0, sq, blk):
                 r1 = min(sq, r0 + blk)
-                out[qs + r0:qs + r1, h] = rel_attn_rows(
+                o, lse = rel_attn_rows(
                     q[qs + r0:qs + r1, h], k_b, v_b, rel[qs + r0:qs + r1, h],
                     np.arange(r0, r1), sq, sk, scale, rel_extent, causal, window_left,
-                    causal_align)
+                    causal_align, return_lse=True)
+                out[qs + r0:qs + r1, h] = o
+                lse_all[h, qs + r0:qs + r1] = lse
     if out_bf16:
         out = round_to_bf16(out)
-    return out
+    return (out, lse_all) if return_lse else out
 
 
 def rel_attn_rows_torch(q_rows, k_b, v_b, rel_rows, q_pos, sq, sk, scale, rel_extent,

@@ -103,3 +103,63 @@ def test_package_ref_rel_attn_matches_reference_output():
         a, b = got[~nan_exp], expected[~nan_exp]
         tol = np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + 1e-5
         assert np.all(np.abs(a - b) <= tol), (name, float(np.abs(a - b).max()))
+
+
+def _split_key_case(sq, sk, split, n_heads=4, kv_heads=2, rel_extent=64, seed=31):
+    """Non-causal rows whose bias is constant along each row (so the bias of a key does not
+    depend on where the key sits), as one full sequence and as the same queries against the
+    key ranges [0, split) and [split, sk) (two sequences of one varlen batch)."""
+    from inkling_fa4.workloads import make_case
+    c = make_case([sq], [sk], n_heads, kv_heads, rel_extent, seed=seed)
+    rel = c.rel.float().numpy()
+    rel = np.repeat(rel[:, :, :1], rel_extent, axis=2)
+    q, k, v = c.q.float().numpy(), c.k.float().numpy(), c.v.float().numpy()
+    full = (q, k, v, rel, np.array([0, sq]), np.array([0, sk]))
+    parts = (np.concatenate([q, q]), k, v, np.concatenate([rel, rel]),
+             np.array([0, sq, 2 * sq]), np.array([0, split, sk]))
+    return full, parts
+
+
+def merge_by_lse(o, lse, sq):
+    """Combine two partial attentions over disjoint key ranges: weights exp(lse_i - lse)."""
+    l1, l2 = lse[:, :sq], lse[:, sq:]
+    lse_all = np.logaddexp(l1, l2)
+    w1 = np.exp(l1 - lse_all).T[:, :, None]
+    w2 = np.exp(l2 - lse_all).T[:, :, None]
+    return w1 * o[:sq] + w2 * o[sq:], lse_all
+
+
+def test_oracle_lse_is_logsumexp_of_the_scores():
+    """The oracle's LSE is log(sum(exp(scores))) of the row's scaled+biased logits."""
+    from inkling_fa4.workloads import make_case
+    c = make_case([40, 7], [40, 7], 2, 1, 16, seed=3)
+    args = (c.q.float().numpy(), c.k.float().numpy(), c.v.float().numpy(), c.rel.float().numpy(),
+            c.cu_q.numpy(), c.cu_k.numpy(), 1 / 128, 16)
+    out, lse = oracle.rel_attn(*args, return_lse=True)
+    np.testing.assert_array_equal(out, oracle.rel_attn(*args))
+    q, k, rel = args[0], args[1], args[3]
+    for h in range(2):
+        for i in range(40):
+            s = q[i, h] @ k[:i + 1, 0].T / 128
+            d = i - np.arange(i + 1)
+            bias = np.where(d < 16, rel[i, h, np.minimum(d, 15)], 0.0)
+            want = np.log(np.sum(np.exp((s + bias).astype(np.float64))))
+            assert abs(lse[h, i] - want) < 1e-5 * max(1.0, abs(want))
+
+
+def test_oracle_lse_merges_split_key_ranges():
+    full, parts = _split_key_case(50, 300, 123)
+    o_full, lse_full = oracle.rel_attn(*full, 1 / 128, 64, causal=False, return_lse=True)
+    o_p, lse_p = oracle.rel_attn(*parts, 1 / 128, 64, causal=False, return_lse=True)
+    o_m, lse_m = merge_by_lse(o_p, lse_p, 50)
+    np.testing.assert_allclose(o_m, o_full, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(lse_m, lse_full, rtol=1e-6, atol=1e-6)
+
+
+def test_oracle_lse_of_empty_rows_is_minus_inf():
+    from inkling_fa4.workloads import make_case
+    c = make_case([3], [0], 2, 2, 8, seed=1)
+    _, lse = oracle.rel_attn(c.q.float().numpy(), c.k.float().numpy(), c.v.float().numpy(),
+                             c.rel.float().numpy(), c.cu_q.numpy(), c.cu_k.numpy(), 1 / 128, 8,
+                             return_lse=True)
+    assert np.all(np.isneginf(lse))
