@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define IFA4_ABI_VERSION 2
+#define IFA4_ABI_VERSION 3
 
 enum {
   IFA4_OK = 0,
@@ -80,6 +80,21 @@ typedef struct IFA4PrefillParams {
    * lse != NULL.  Not in the reference; callers merge split attention with it. */
   float* lse;
   int64_t lse_stride_h, lse_stride_t;
+  /* Optional paged KV cache, used when block_table != NULL.  Not in the reference (its
+   * serving-stack caller keeps K/V in 16-token pages).  k and v then point to caches
+   * [num_pages, page_size, kv_heads, head_dim] with element strides (k_stride_page,
+   * k_stride_t, k_stride_h, 1) (likewise v), and key j of sequence b sits in page
+   * block_table[b * block_table_stride + j / page_size], slot j % page_size.  Key counts
+   * still come from cu_seqlens_k (cu_seqlens_k[b+1] - cu_seqlens_k[b]); total_k is ignored.
+   * page_size is a power of two >= 16; page strides are positive multiples of 8 elements.
+   * Each sequence's table row must hold ceil(keys / page_size) entries; an entry outside
+   * [0, num_pages) reads as zero keys and values.  Cache slots past a sequence's last key are
+   * never used, whatever they hold (NaN included). */
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int64_t k_stride_page, v_stride_page;
+  int32_t page_size;
+  int32_t num_pages;
 } IFA4PrefillParams;
 
 /* Prefill.  Replaces the per-sequence launch loop of inkling_fa4_rel_attention_triton
@@ -122,6 +137,12 @@ typedef struct IFA4DecodeParams {
   int32_t chunk_len;        /* 0 = automatic; otherwise a multiple of 64               */
   float* lse;               /* optional, as in IFA4PrefillParams (token = the query row) */
   int64_t lse_stride_h, lse_stride_t;
+  /* optional paged KV cache, as in IFA4PrefillParams */
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int64_t k_stride_page, v_stride_page;
+  int32_t page_size;
+  int32_t num_pages;
 } IFA4DecodeParams;
 
 /* Decode.  Replaces inkling_fa4_rel_attention_decode_triton

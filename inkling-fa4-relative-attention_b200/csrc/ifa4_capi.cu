@@ -120,6 +120,39 @@ int encode_rows_heads_dims(CUtensorMap* map, const void* base, int64_t rows, int
   return IFA4_OK;
 }
 
+// Paged cache [pages, page_size, heads, 128] bf16 with element strides (sp, st, sh): 4-D boxes
+// of 64 dims x 1 head x box_rows x 1 page, 128-byte swizzle; out-of-range pages read as zero.
+int encode_paged(CUtensorMap* map, const void* base, int64_t pages, int64_t page_size,
+                 int64_t heads, int64_t sp, int64_t st, int64_t sh, uint32_t box_rows,
+                 const char* name) {
+  EncodeTiledFn fn;
+  int rc = get_encode_fn(&fn);
+  if (rc) return rc;
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(page_size),
+                        static_cast<cuuint64_t>(pages)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(sh) * 2, static_cast<cuuint64_t>(st) * 2,
+                           static_cast<cuuint64_t>(sp) * 2};
+  cuuint32_t box[4] = {64, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(IFA4_ERR_UNSUPPORTED,
+                "cuTensorMapEncodeTiled(%s, paged) failed with CUresult %d (pages=%lld "
+                "page_size=%lld heads=%lld stride_page=%lld stride_t=%lld stride_h=%lld)",
+                name, static_cast<int>(r), static_cast<long long>(pages),
+                static_cast<long long>(page_size), static_cast<long long>(heads),
+                static_cast<long long>(sp), static_cast<long long>(st), static_cast<long long>(sh));
+  return IFA4_OK;
+}
+
+int log2_exact(int64_t x) {
+  int s = 0;
+  while ((int64_t{1} << s) < x) ++s;
+  return s;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Checks shared by prefill and decode.
@@ -156,7 +189,52 @@ int validate_common(const P* p, const char* what) {
   if (p->rel_stride_t < 0 || p->rel_stride_h < 0)
     return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: negative rel strides", what);
   if (p->batch > 65535) return fail(IFA4_ERR_UNSUPPORTED, "%s: batch > 65535", what);
+  if (p->block_table != nullptr) {
+    if (p->page_size < 16 || p->page_size > (1 << 20) || (p->page_size & (p->page_size - 1)) != 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: page_size %d must be a power of two in [16, 2^20]",
+                  what, p->page_size);
+    if (p->num_pages <= 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: num_pages must be > 0", what);
+    if (p->block_table_stride < 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT, "%s: negative block_table_stride", what);
+    if (p->k_stride_page <= 0 || p->k_stride_page % 8 != 0 || p->v_stride_page <= 0 ||
+        p->v_stride_page % 8 != 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT,
+                  "%s: k/v page strides must be positive multiples of 8 elements", what);
+  }
   return IFA4_OK;
+}
+
+// Tensor maps for K and V: [total_k, kv_heads, 128] with boxes of `tile_rows` rows, or the
+// paged caches with boxes of min(page_size, tile_rows) rows.
+template <class P>
+int encode_kv(const P* p, uint32_t tile_rows, CUtensorMap* tk, CUtensorMap* tv) {
+  int rc;
+  if (p->block_table != nullptr) {
+    const uint32_t box = p->page_size < static_cast<int>(tile_rows) ? p->page_size : tile_rows;
+    if ((rc = encode_paged(tk, p->k, p->num_pages, p->page_size, p->kv_heads, p->k_stride_page,
+                           p->k_stride_t, p->k_stride_h, box, "k")))
+      return rc;
+    return encode_paged(tv, p->v, p->num_pages, p->page_size, p->kv_heads, p->v_stride_page,
+                        p->v_stride_t, p->v_stride_h, box, "v");
+  }
+  const int64_t krows = p->total_k > 0 ? p->total_k : 1;
+  if ((rc = encode_rows_heads_dims(tk, p->k, krows, p->kv_heads, p->k_stride_t, p->k_stride_h,
+                                   tile_rows, "k")))
+    return rc;
+  return encode_rows_heads_dims(tv, p->v, krows, p->kv_heads, p->v_stride_t, p->v_stride_h,
+                                tile_rows, "v");
+}
+
+// Kernel-side paged fields (no-ops without a block table).
+template <class P, class A>
+void fill_paged(const P* p, uint32_t tile_rows, A* a) {
+  a->block_table = p->block_table;
+  if (p->block_table == nullptr) return;
+  a->bt_stride = p->block_table_stride;
+  a->page_shift = log2_exact(p->page_size);
+  a->box_shift = log2_exact(p->page_size < static_cast<int>(tile_rows) ? p->page_size : tile_rows);
+  a->num_pages = p->num_pages;
 }
 
 }  // namespace
@@ -171,7 +249,9 @@ const char* ifa4_prefill_tile_config_name(int32_t tile_config) {
   static const char* names[ifa4::kPrefillNumTileConfigs] = {
       "sm100_q2x128_kv128_d128_ws12_default", "sm100_q2x128_kv128_d128_ws12_emu0of16",
       "sm100_q2x128_kv128_d128_ws12_emu2of16", "sm100_q2x128_kv128_d128_ws12_emu4of16",
-      "sm100_q2x128_kv128_d128_ws12_emu6of16", "sm100_q2x128_kv128_d128_ws12_emu8of16"};
+      "sm100_q2x128_kv128_d128_ws12_emu6of16", "sm100_q2x128_kv128_d128_ws12_emu8of16",
+      "sm100_q2x128_kv128_d128_ws12_h2x16of16", "sm100_q2x128_kv128_d128_ws12_h2x8of16",
+      "sm100_q2x128_kv128_d128_ws12_emu4h2x8of16"};
   if (tile_config < 0 || tile_config >= ifa4::kPrefillNumTileConfigs) return "";
   return names[tile_config];
 }
@@ -182,11 +262,10 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   if (rc) return rc;
   if (ifa4::prefill_emulated_exp_columns(p->tile_config) < 0)
     return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d unknown", p->tile_config);
+  if (p->block_table != nullptr && !ifa4::prefill_paged_tile_config_ok(p->tile_config))
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d has no paged-cache variant (0, 1, 3)",
+                p->tile_config);
   if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
-  if (p->total_k == 0) {
-    // no keys at all: every row has no visible key -> zeros (handled by the kernel too, but
-    // the K/V tensor maps need at least one row)
-  }
   int* status = nullptr;
   if ((rc = device_status_ptr(&status))) return rc;
 
@@ -212,19 +291,18 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   a.lse = p->lse;
   a.lse_sh = p->lse_stride_h;
   a.lse_st = p->lse_stride_t;
+  fill_paged(p, 128, &a);
+  a.v = static_cast<const uint16_t*>(p->v);
+  a.v_st = p->v_stride_t;
+  a.v_sh = p->v_stride_h;
+  a.v_sp = p->v_stride_page;
   a.status = status;
 
   CUtensorMap tq, tk, tv;
-  const int64_t krows = p->total_k > 0 ? p->total_k : 1;
   if ((rc = encode_rows_heads_dims(&tq, p->q, p->total_q, p->n_heads, p->q_stride_t,
                                    p->q_stride_h, 128, "q")))
     return rc;
-  if ((rc = encode_rows_heads_dims(&tk, p->k, krows, p->kv_heads, p->k_stride_t, p->k_stride_h,
-                                   128, "k")))
-    return rc;
-  if ((rc = encode_rows_heads_dims(&tv, p->v, krows, p->kv_heads, p->v_stride_t, p->v_stride_h,
-                                   128, "v")))
-    return rc;
+  if ((rc = encode_kv(p, 128, &tk, &tv))) return rc;
   const int rows_per_cta = a.pair_heads ? 128 : 256;
   int64_t max_sq = p->max_seqlen_q > 0 ? p->max_seqlen_q : p->total_q;
   if (max_sq > p->total_q) max_sq = p->total_q;
@@ -243,8 +321,11 @@ static int decode_plan(const IFA4DecodeParams* p, int* num_splits, int* chunk_le
   const int group = p->n_heads / p->kv_heads;
   const int hpc = group < 16 ? group : 16;
   const int head_blocks = (group + hpc - 1) / hpc;
-  int64_t max_sk = p->max_seqlen_k > 0 ? p->max_seqlen_k : p->total_k;
-  if (max_sk > p->total_k) max_sk = p->total_k;
+  const int64_t key_cap = p->block_table != nullptr
+                              ? static_cast<int64_t>(p->num_pages) * p->page_size
+                              : p->total_k;
+  int64_t max_sk = p->max_seqlen_k > 0 ? p->max_seqlen_k : key_cap;
+  if (max_sk > key_cap) max_sk = key_cap;
   if (max_sk < 1) max_sk = 1;
   int chunk = p->chunk_len;
   int splits = p->num_splits;
@@ -346,15 +427,10 @@ int ifa4_decode_launch(const IFA4DecodeParams* p, void* workspace, size_t worksp
   a.lse = p->lse;
   a.lse_sh = p->lse_stride_h;
   a.lse_st = p->lse_stride_t;
+  fill_paged(p, 64, &a);
   a.status = status;
   CUtensorMap tk, tv;
-  const int64_t krows = p->total_k > 0 ? p->total_k : 1;
-  if ((rc = encode_rows_heads_dims(&tk, p->k, krows, p->kv_heads, p->k_stride_t, p->k_stride_h,
-                                   64, "k")))
-    return rc;
-  if ((rc = encode_rows_heads_dims(&tv, p->v, krows, p->kv_heads, p->v_stride_t, p->v_stride_h,
-                                   64, "v")))
-    return rc;
+  if ((rc = encode_kv(p, 64, &tk, &tv))) return rc;
   cudaError_t e = ifa4::launch_decode_sm100(a, tk, tv, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return IFA4_OK;

@@ -14,6 +14,13 @@
 // writes the bf16 output, otherwise a normalised fp32 partial and its log2-sum-exp, which
 // rel_attn_decode_combine_kernel merges.
 //
+// Paged KV cache (kPaged): the whole producer warp runs, fetching the next tile's page numbers
+// from the block table while the current tile is issued; a 64-key tile is loaded as 64 / box
+// units of box = min(page_size, 64) rows (one 4-D TMA box per unit, tensor and 64-dim half),
+// units past the sequence's end load zeros, and tiles start at the window's first key rounded
+// down to the box size.  V values of keys past the sequence's end (unused cache slots, possibly
+// NaN) are zeroed in the B fragments before the P.V product.
+//
 // Decode is bandwidth-bound (about 4 FLOP per K/V byte for a group of 4), so the roofline is
 // HBM; the warp-level MMA keeps the issue cost per key small.  Semantics follow the oracle
 // (reference.py:27-39) for sq = 1.
@@ -77,9 +84,10 @@ __device__ __forceinline__ uint32_t sw128_addr(uint32_t base, int row, int chunk
 }
 
 struct SeqInfo {
-  int q_row, k_start, sk, lo, hi, nchunks;
+  int q_row, k_start, sk, lo, hi, base, nchunks;  // chunks start at base + c * chunk_len
 };
 
+template <bool kPaged>
 __device__ __forceinline__ SeqInfo seq_info(const DecodeKernelArgs& a, int b) {
   SeqInfo s;
   s.q_row = a.cu_q[b];
@@ -89,10 +97,12 @@ __device__ __forceinline__ SeqInfo seq_info(const DecodeKernelArgs& a, int b) {
   s.hi = s.sk;
   if (a.causal) s.hi = min(s.hi, ms + 1);
   s.lo = a.window_left >= 0 ? max(0, ms - a.window_left) : 0;
-  s.nchunks = s.hi > s.lo ? (s.hi - s.lo + a.chunk_len - 1) / a.chunk_len : 0;
+  s.base = kPaged ? s.lo & ~((1 << a.box_shift) - 1) : s.lo;
+  s.nchunks = s.hi > s.lo ? (s.hi - s.base + a.chunk_len - 1) / a.chunk_len : 0;
   return s;
 }
 
+template <bool kPaged>
 __global__ void __launch_bounds__(kThreads, 2)
     rel_attn_decode_kernel(const __grid_constant__ DecodeKernelArgs a,
                            const __grid_constant__ CUtensorMap tm_k,
@@ -110,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int h0 = kvh * a.group + hblk * a.heads_per_cta;
   const int nh = min(a.heads_per_cta, a.group - hblk * a.heads_per_cta);
   const int b = blockIdx.z;
-  const SeqInfo si = seq_info(a, b);
+  const SeqInfo si = seq_info<kPaged>(a, b);
   const int bs = a.align_bottom_right ? si.sk - 1 : 1 - si.sk;  // bias distance at key 0
 
   if (threadIdx.x == 0) {
@@ -131,7 +141,67 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-  if (warp == kConsumerWarps) {
+  if (kPaged && warp == kConsumerWarps) {
+    // ---------------------------------------------------------------- paged TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
+    const uint64_t pol = l2_policy_evict_first();
+    const int box = 1 << a.box_shift;
+    const int units = kTileKeys >> a.box_shift;
+    const int page_mask = (1 << a.page_shift) - 1;
+    const int32_t* bt = a.block_table + static_cast<long long>(b) * a.bt_stride;
+    // page of unit `lane` of the tile at key t0; -1 past the end or for an invalid entry
+    auto unit_block = [&](int t0) {
+      const int key = t0 + lane * box;
+      int blk = -1;
+      if (lane < units && key < si.sk) {
+        blk = __ldg(bt + (key >> a.page_shift));
+        if (blk < 0 || blk >= a.num_pages) blk = -1;
+      }
+      return blk;
+    };
+    uint32_t n = 0;
+    int c = split;
+    int t0 = si.base + c * a.chunk_len;
+    int blk = c < si.nchunks ? unit_block(t0) : -1;
+    while (c < si.nchunks) {
+      const int c1 = min(si.hi, si.base + c * a.chunk_len + a.chunk_len);
+      int nc = c, nt0 = t0 + kTileKeys;  // the tile after this one, in consumer order
+      if (nt0 >= c1) {
+        nc = c + gridDim.x;
+        nt0 = si.base + nc * a.chunk_len;
+      }
+      const int nblk = nc < si.nchunks ? unit_block(nt0) : -1;  // in flight across the wait
+      const uint32_t st = n % kStages;
+      if (!mbar_wait_warp(&bars->empty[st], ((n / kStages) & 1) ^ 1, ab)) break;
+      if (lane == 0) mbar_arrive_expect_tx(&bars->full[st], kStageBytes);
+      __syncwarp();
+      if (lane < units) {
+        uint8_t* base = smem + st * kStageBytes + lane * box * 128;
+        const int in_page = (t0 + lane * box) & page_mask;
+        const int page = blk >= 0 ? blk : a.num_pages;  // out of range: TMA writes zeros
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          tma_load_4d_hint(base + hf * kHalf, &tm_k, &bars->full[st], hf * 64, kvh, in_page,
+                           page, pol);
+          tma_load_4d_hint(base + kKVTile + hf * kHalf, &tm_v, &bars->full[st], hf * 64, kvh,
+                           in_page, page, pol);
+        }
+      }
+      ++n;
+      c = nc;
+      t0 = nt0;
+      blk = nblk;
+    }
+    if (lane == 0) {  // drain the last use of every stage
+      for (uint32_t i = 0; i < kStages && i < n; ++i) {
+        const uint32_t last = n - 1 - i;
+        mbar_wait(&bars->full[last % kStages], (last / kStages) & 1, ab);
+      }
+    }
+  } else if (warp == kConsumerWarps) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
@@ -140,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t n = 0;
       bool ok = true;
       for (int c = split; c < si.nchunks && ok; c += gridDim.x) {
-        const int c0 = si.lo + c * a.chunk_len;
+        const int c0 = si.base + c * a.chunk_len;
         const int c1 = min(si.hi, c0 + a.chunk_len);
         for (int t0 = c0; t0 < c1; t0 += kTileKeys, ++n) {
           const uint32_t st = n % kStages;
@@ -190,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint32_t n = 0;
     bool ok = true;
     for (int c = split; c < si.nchunks && ok; c += gridDim.x) {
-      const int c0 = si.lo + c * a.chunk_len;
+      const int c0 = si.base + c * a.chunk_len;
       const int c1 = min(si.hi, c0 + a.chunk_len);
       for (int t0 = c0; t0 < c1; t0 += kTileKeys, ++n) {
         const uint32_t st = n % kStages;
@@ -271,6 +341,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         // ---- O += P V  (V^T fragments via transposed ldmatrix).  The bias/mask code above
         // branches per lane; ldmatrix/mma are .sync.aligned: reconverge the warp first.
+        // Paged cache: keys past the sequence's end may sit in unused (even NaN) cache slots;
+        // this lane's B fragments hold keys kt + 2qd (+1) (b0, b2; low, high half) and
+        // kt + 8 + 2qd (+1) (b1, b3).
+        uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
+        if (kPaged && kt + 16 > si.sk) {
+          const int k0 = kt + 2 * qd;
+          vm0 = (k0 < si.sk ? 0x0000ffffu : 0u) | (k0 + 1 < si.sk ? 0xffff0000u : 0u);
+          vm1 = (k0 + 8 < si.sk ? 0x0000ffffu : 0u) | (k0 + 9 < si.sk ? 0xffff0000u : 0u);
+        }
         __syncwarp();
         {
           const int mi = lane >> 3;
@@ -279,6 +358,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int dt = 0; dt < 16; dt += 2) {
             uint32_t b0, b1, b2, b3;
             ldsm_x4_t(sw128_addr(vbase, vrow, dt + (mi >> 1)), b0, b1, b2, b3);
+            if (kPaged) {
+              b0 &= vm0;
+              b1 &= vm1;
+              b2 &= vm0;
+              b3 &= vm1;
+            }
             mma_bf16(o[dt], pa, b0, b1);
             mma_bf16(o[dt + 1], pa, b2, b3);
           }
@@ -388,16 +473,24 @@ cudaError_t launch_decode_sm100(const DecodeKernelArgs& args, const CUtensorMap&
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode::rel_attn_decode_kernel,
+    cudaError_t e = cudaFuncSetAttribute(decode::rel_attn_decode_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(decode::kSmemAlloc));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(decode::rel_attn_decode_kernel<true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(decode::kSmemAlloc));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   const int head_blocks = (args.group + args.heads_per_cta - 1) / args.heads_per_cta;
   dim3 grid(args.num_splits, args.kv_heads * head_blocks, args.batch);
-  decode::rel_attn_decode_kernel<<<grid, decode::kThreads, decode::kSmemAlloc, stream>>>(
-      args, tm_k, tm_v);
+  if (args.block_table != nullptr)
+    decode::rel_attn_decode_kernel<true><<<grid, decode::kThreads, decode::kSmemAlloc, stream>>>(
+        args, tm_k, tm_v);
+  else
+    decode::rel_attn_decode_kernel<false><<<grid, decode::kThreads, decode::kSmemAlloc, stream>>>(
+        args, tm_k, tm_v);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || args.num_splits == 1) return e;
   dim3 cgrid(args.n_heads, args.batch);

@@ -27,6 +27,13 @@ struct PrefillKernelArgs {
   float scale_log2;          // softmax_scale * log2(e)
   float* lse;                // optional natural-log LSE, [h * lse_sh + token * lse_st]
   long long lse_sh, lse_st;
+  // paged KV cache (kernels instantiated with kPaged): K/V tensor maps are 4-D
+  // {128 dims, kv_heads, page_size, num_pages}; tiles load in units of 2^box_shift rows
+  const int32_t* block_table;
+  long long bt_stride;
+  int page_shift, box_shift, num_pages;
+  const uint16_t* v;         // V cache base (partial last unit copied with plain loads)
+  long long v_st, v_sh, v_sp;
   int* status;
 };
 
@@ -46,10 +53,12 @@ constexpr int kPrefillNumTileConfigs = 9;
 int prefill_emulated_exp_columns(int tile_config);  // -1 for an unknown id
 
 // Launches the tcgen05 prefill kernel variant of `tile_config`.  Returns a cudaError_t.
+// With a paged cache (args.block_table != nullptr) only tile configs 0, 1 and 3 exist.
 cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                  int q_slots, int tile_config, int max_seqlen_q,
                                  cudaStream_t stream);
+bool prefill_paged_tile_config_ok(int tile_config);
 
 struct DecodeKernelArgs {
   const uint16_t* q;
@@ -71,6 +80,9 @@ struct DecodeKernelArgs {
   float* ws_lse;             // [batch, n_heads, num_splits]      (num_splits > 1)
   float* lse;                // optional natural-log LSE output
   long long lse_sh, lse_st;
+  const int32_t* block_table;  // paged KV cache, as in PrefillKernelArgs
+  long long bt_stride;
+  int page_shift, box_shift, num_pages;
   int* status;
 };
 

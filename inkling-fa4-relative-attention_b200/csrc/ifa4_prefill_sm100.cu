@@ -15,6 +15,16 @@
 //               when the running max grows by more than 2^8), P written back to TMEM as bf16
 //               over the first 64 columns of S, epilogue O / l -> bf16 -> global.
 //
+// Paged KV cache (kPaged): K/V come from [num_pages, page_size, kv_heads, 128] caches through
+// a block table.  The whole of warp 0 produces: lanes fetch the page numbers of the next KV tile
+// while the current one is issued, and each 128-key tile is loaded as 128 / box units of box =
+// min(page_size, 128) rows, one 4-D TMA box per unit and 64-dim half, into the same swizzled
+// layout as the contiguous path.  Units at or past the sequence's end load zeros (an
+// out-of-range page coordinate).  The unit that holds the sequence's last key is copied into
+// the V stage by the warp itself with its rows past the last key zeroed: P is 0 there, but a
+// NaN left in an unused cache slot would still turn 0 * NaN into NaN in the P.V product
+// (unused K rows are harmless: the mask replaces their scores).
+//
 // Causal and sliding-window masks prune KV tiles before any load: the loop covers exactly the
 // tiles [j_lo, j_hi) that intersect the union of the two sub-tiles' visible key ranges; the
 // per-element mask runs only for rows whose range does not cover the whole tile.
@@ -119,6 +129,115 @@ __device__ __forceinline__ TileInfo tile_info(const PrefillKernelArgs& a, int qt
   return t;
 }
 
+// Producer for a paged KV cache: run by all 32 lanes of warp 0 (see the file comment).
+__device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_t* smem,
+                                              Bars* bars, const CUtensorMap* tm_q,
+                                              const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                                              int hslot, int b, int q_start, int sq, int sk,
+                                              int n_qt, int lane, const AbortCtx& ab) {
+  uint32_t qc = 0, kc = 0, vc = 0;
+  const uint64_t pol_kv = l2_policy_evict_last();
+  const uint64_t pol_q = l2_policy_evict_first();
+  const int box = 1 << a.box_shift;
+  const int units = kBN >> a.box_shift;
+  const int page_mask = (1 << a.page_shift) - 1;
+  const int32_t* bt = a.block_table + static_cast<long long>(b) * a.bt_stride;
+  bool ok = true;
+  for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+    const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+    if (t.n_kv == 0) continue;
+    if (!(ok = mbar_wait_warp(&bars->q_empty, (qc & 1) ^ 1, ab))) break;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->q_full, 2 * kTile);
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d_hint(smem + kSmemQ + s * kTile + hf * kHalf, tm_q, &bars->q_full, hf * 64,
+                           t.head[s], q_start + t.row0[s], pol_q);
+    }
+    ++qc;
+    // page of unit `lane` of KV tile j; -1 past the sequence's end or for an entry outside
+    // [0, num_pages)
+    auto unit_block = [&](int j) {
+      const int key = (t.j_lo + j) * kBN + lane * box;
+      int blk = -1;
+      if (lane < units && key < sk) {
+        blk = __ldg(bt + (key >> a.page_shift));
+        if (blk < 0 || blk >= a.num_pages) blk = -1;
+      }
+      return blk;
+    };
+    int blk = unit_block(0);
+    for (int j = 0; j < t.n_kv; ++j) {
+      const int key0 = (t.j_lo + j) * kBN;
+      const int blk_next = j + 1 < t.n_kv ? unit_block(j + 1) : -1;  // in flight across waits
+      const int in_page = (key0 + lane * box) & page_mask;
+      const int page = blk >= 0 ? blk : a.num_pages;  // out of range: TMA writes zeros
+      const uint32_t ks = kc & 1;
+      if (!(ok = mbar_wait_warp(&bars->k_empty[ks], ((kc >> 1) & 1) ^ 1, ab))) break;
+      if (lane == 0) mbar_arrive_expect_tx(&bars->k_full[ks], kTile);
+      __syncwarp();
+      if (lane < units) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d_hint(smem + kSmemK + ks * kTile + hf * kHalf + lane * box * 128, tm_k,
+                           &bars->k_full[ks], hf * 64, t.kvh, in_page, page, pol_kv);
+      }
+      ++kc;
+      const uint32_t vs = vc & 1;
+      if (!(ok = mbar_wait_warp(&bars->v_empty[vs], ((vc >> 1) & 1) ^ 1, ab))) break;
+      // the unit holding the sequence's last key, unless that key ends the unit
+      const int pu = (key0 < sk && sk < key0 + kBN && (sk & (box - 1)) != 0)
+                         ? (sk - key0) >> a.box_shift : -1;
+      uint32_t v_bytes = kTile;
+      if (pu >= 0) {
+        const int pblk = __shfl_sync(0xffffffffu, blk, pu);
+        const int pkey = key0 + pu * box;
+        const int nvalid = sk - pkey;
+        const uint16_t* src = a.v + static_cast<long long>(pblk < 0 ? 0 : pblk) * a.v_sp +
+                              static_cast<long long>(pkey & page_mask) * a.v_st +
+                              static_cast<long long>(t.kvh) * a.v_sh;
+        uint8_t* dst = smem + kSmemV + vs * kTile;
+#pragma unroll 4
+        for (int i = lane; i < box * 16; i += 32) {
+          const int r = i >> 4, ch = i & 15;
+          uint4 val = make_uint4(0u, 0u, 0u, 0u);
+          if (r < nvalid && pblk >= 0) val = ldg_nc_v4(src + static_cast<long long>(r) * a.v_st + ch * 8);
+          const int row = pu * box + r;
+          *reinterpret_cast<uint4*>(dst + (ch >> 3) * kHalf + row * 128 +
+                                    (((ch & 7) ^ (row & 7)) << 4)) = val;
+        }
+        fence_proxy_async_smem();  // the UMMA reads these bytes through the async proxy
+        __syncwarp();
+        v_bytes -= static_cast<uint32_t>(box) * 256u;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&bars->v_full[vs], v_bytes);
+      __syncwarp();
+      if (lane < units && lane != pu) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d_hint(smem + kSmemV + vs * kTile + hf * kHalf + lane * box * 128, tm_v,
+                           &bars->v_full[vs], hf * 64, t.kvh, in_page, page, pol_kv);
+      }
+      ++vc;
+      blk = blk_next;
+    }
+  }
+  // Drain: every issued load has completed before the CTA may exit.
+  if (lane == 0) {
+    if (qc > 0) mbar_wait(&bars->q_full, (qc - 1) & 1, ab);
+    for (uint32_t i = 0; i < 2 && i < kc; ++i) {
+      const uint32_t last = kc - 1 - i;
+      mbar_wait(&bars->k_full[last & 1], (last >> 1) & 1, ab);
+    }
+    for (uint32_t i = 0; i < 2 && i < vc; ++i) {
+      const uint32_t last = vc - 1 - i;
+      mbar_wait(&bars->v_full[last & 1], (last >> 1) & 1, ab);
+    }
+  }
+}
+
 __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr) {
   const uint64_t qd = sdesc_sw128(q_addr, 16, 1024);
   const uint64_t kd = sdesc_sw128(k_addr, 16, 1024);
@@ -139,7 +258,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint3
   }
 }
 
-template <int kEmu, int kHalf2>
+template <int kEmu, int kHalf2, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
                             const __grid_constant__ CUtensorMap tm_q,
@@ -194,7 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = bars->tmem_base;
   const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
   if (warp < 4) {
-   if (warp == 0) {
+   if (kPaged && warp == 0) {
+    produce_paged(a, smem, bars, &tm_q, &tm_k, &tm_v, hslot, b, q_start, sq, sk, n_qt, lane, ab);
+   } else if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t qc = 0, kc = 0, vc = 0;
@@ -601,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace prefill
 
 namespace {
-template <int kEmu, int kHalf2>
+template <int kEmu, int kHalf2, bool kPaged>
 cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
                            cudaStream_t stream) {
@@ -612,13 +733,13 @@ cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu, kHalf2>,
+    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(prefill::kSmemAlloc));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  prefill::rel_attn_prefill_kernel<kEmu, kHalf2>
+  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>
       <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
   return cudaGetLastError();
 }
@@ -628,6 +749,10 @@ cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_
 static const int kVariants[kPrefillNumTileConfigs][2] = {
     {kPrefillDefaultEmu, kPrefillDefaultHalf2}, {0, 0}, {2, 0}, {4, 0}, {6, 0}, {8, 0},
     {0, 16}, {0, 8}, {4, 8}};
+
+bool prefill_paged_tile_config_ok(int tile_config) {
+  return tile_config == 0 || tile_config == 1 || tile_config == 3;
+}
 
 int prefill_emulated_exp_columns(int tile_config) {
   if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return -1;
@@ -650,8 +775,13 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
     emu = (args.window_left < 0 && max_seqlen_q >= 16384) ? 4 : 0;
     h2 = 0;
   }
+  if (args.block_table != nullptr) {  // paged cache: the two variants the automatic choice uses
+    if (emu == 0 && h2 == 0) return launch_variant<0, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
+    if (emu == 4 && h2 == 0) return launch_variant<4, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
+    return cudaErrorInvalidValue;
+  }
 #define IFA4_VARIANT(E, H) \
-  if (emu == E && h2 == H) return launch_variant<E, H>(args, tm_q, tm_k, tm_v, grid, stream);
+  if (emu == E && h2 == H) return launch_variant<E, H, false>(args, tm_q, tm_k, tm_v, grid, stream);
   IFA4_VARIANT(0, 0)
   IFA4_VARIANT(2, 0)
   IFA4_VARIANT(4, 0)

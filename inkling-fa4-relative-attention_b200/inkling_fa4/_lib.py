@@ -19,7 +19,7 @@ IFA4_ERR_DEVICE_TIMEOUT = -5
 IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0
-ABI_VERSION = 2
+ABI_VERSION = 3
 NOALLOC_DECODE_SCRATCH_BYTES = 16 * 1024 * 1024
 
 EXPORTED_SYMBOLS = (
@@ -55,6 +55,9 @@ class PrefillParams(ctypes.Structure):
         ("max_seqlen_q", ctypes.c_int32), ("dtype", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float), ("tile_config", ctypes.c_int32),
         ("lse", ctypes.c_void_p), ("lse_stride_h", ctypes.c_int64), ("lse_stride_t", ctypes.c_int64),
+        ("block_table", ctypes.c_void_p), ("block_table_stride", ctypes.c_int64),
+        ("k_stride_page", ctypes.c_int64), ("v_stride_page", ctypes.c_int64),
+        ("page_size", ctypes.c_int32), ("num_pages", ctypes.c_int32),
     ]
 
 
@@ -65,6 +68,9 @@ class DecodeParams(ctypes.Structure):
         ("softmax_scale", ctypes.c_float), ("num_splits", ctypes.c_int32),
         ("chunk_len", ctypes.c_int32),
         ("lse", ctypes.c_void_p), ("lse_stride_h", ctypes.c_int64), ("lse_stride_t", ctypes.c_int64),
+        ("block_table", ctypes.c_void_p), ("block_table_stride", ctypes.c_int64),
+        ("k_stride_page", ctypes.c_int64), ("v_stride_page", ctypes.c_int64),
+        ("page_size", ctypes.c_int32), ("num_pages", ctypes.c_int32),
     ]
 
 

@@ -23,9 +23,13 @@ def _tma_ready(t: torch.Tensor) -> torch.Tensor:
 
 
 def _check_inputs(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, n_heads, kv_heads,
-                  head_dim, window_size, causal_align):
-    for nm, t in (("q", q), ("k", k), ("v", v), ("rel_logits", rel_logits),
-                  ("cu_seqlens_q", cu_q), ("cu_seqlens_k", cu_k)):
+                  head_dim, window_size, causal_align, block_table=None):
+    paged = block_table is not None
+    tensors = [("q", q), ("k", k), ("v", v), ("rel_logits", rel_logits),
+               ("cu_seqlens_q", cu_q), ("cu_seqlens_k", cu_k)]
+    if paged:
+        tensors.append(("block_table", block_table))
+    for nm, t in tensors:
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name}: {nm} must be a torch.Tensor")
         if not t.is_cuda:
@@ -35,25 +39,37 @@ def _check_inputs(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, n_heads, kv
     for nm, t in (("q", q), ("k", k), ("v", v), ("rel_logits", rel_logits)):
         if t.dtype != torch.bfloat16:
             raise TypeError(f"{name}: {nm} must be bfloat16, got {t.dtype}")
-        if t.dim() != 3:
-            raise ValueError(f"{name}: {nm} must be 3-D")
+        want = 4 if paged and nm in ("k", "v") else 3
+        if t.dim() != want:
+            raise ValueError(f"{name}: {nm} must be {want}-D"
+                             + (" [num_pages, page_size, kv_heads, head_dim]" if want == 4 else ""))
     for nm, t in (("cu_seqlens_q", cu_q), ("cu_seqlens_k", cu_k)):
         if t.dtype != torch.int32 or t.dim() != 1 or t.numel() < 1:
             raise ValueError(f"{name}: {nm} must be a non-empty 1-D int32 tensor")
     if cu_q.numel() != cu_k.numel():
         raise ValueError(f"{name}: cu_seqlens_q and cu_seqlens_k differ in length")
+    hdim = 2 if paged else 1  # kv head dimension of k / v
     if n_heads is None:
         n_heads = q.shape[1]
     if kv_heads is None:
-        kv_heads = k.shape[1]
-    if n_heads != q.shape[1] or kv_heads != k.shape[1] or v.shape[1] != kv_heads:
+        kv_heads = k.shape[hdim]
+    if n_heads != q.shape[1] or kv_heads != k.shape[hdim] or v.shape[hdim] != kv_heads:
         raise ValueError(f"{name}: head counts disagree with tensor shapes")
     if n_heads % kv_heads != 0:
         raise ValueError(f"{name}: n_heads {n_heads} not a multiple of kv_heads {kv_heads}")
-    if head_dim != HEAD_DIM or q.shape[2] != HEAD_DIM or k.shape[2] != HEAD_DIM or v.shape[2] != HEAD_DIM:
+    if head_dim != HEAD_DIM or q.shape[-1] != HEAD_DIM or k.shape[-1] != HEAD_DIM or v.shape[-1] != HEAD_DIM:
         raise ValueError(f"{name}: head_dim must be {HEAD_DIM}")
-    if k.shape[0] != v.shape[0]:
-        raise ValueError(f"{name}: k and v differ in token count")
+    if k.shape[:-1] != v.shape[:-1]:
+        raise ValueError(f"{name}: k and v differ in shape")
+    if paged:
+        ps = k.shape[1]
+        if ps < 16 or ps & (ps - 1):
+            raise ValueError(f"{name}: page_size {ps} must be a power of two >= 16")
+        if (block_table.dtype != torch.int32 or block_table.dim() != 2
+                or block_table.shape[0] != cu_q.numel() - 1
+                or (block_table.shape[1] > 1 and block_table.stride(1) != 1)):
+            raise ValueError(f"{name}: block_table must be int32 [batch, max_pages] with unit "
+                             "last stride")
     if rel_logits.shape[0] != q.shape[0] or rel_logits.shape[1] != n_heads:
         raise ValueError(f"{name}: rel_logits must be [total_q, n_heads, >=rel_extent]")
     rel_extent = int(rel_extent)
@@ -84,16 +100,25 @@ def _fill_lse(p, lse):
 
 
 def _fill_common(p, q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
-                 window_left, causal_align):
+                 window_left, causal_align, block_table=None):
     p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
     p.rel, p.out = rel.data_ptr(), out.data_ptr()
     p.cu_seqlens_q, p.cu_seqlens_k = cu_q.data_ptr(), cu_k.data_ptr()
     p.q_stride_t, p.q_stride_h = q.stride(0), q.stride(1)
-    p.k_stride_t, p.k_stride_h = k.stride(0), k.stride(1)
-    p.v_stride_t, p.v_stride_h = v.stride(0), v.stride(1)
+    p.k_stride_t, p.k_stride_h = k.stride(-3), k.stride(-2)
+    p.v_stride_t, p.v_stride_h = v.stride(-3), v.stride(-2)
     p.rel_stride_t, p.rel_stride_h = rel.stride(0), rel.stride(1)
     p.out_stride_t, p.out_stride_h = out.stride(0), out.stride(1)
-    p.total_q, p.total_k = q.shape[0], k.shape[0]
+    p.total_q = q.shape[0]
+    if block_table is None:
+        p.total_k = k.shape[0]
+        p.block_table, p.block_table_stride = None, 0
+        p.k_stride_page = p.v_stride_page = p.page_size = p.num_pages = 0
+    else:
+        p.total_k = k.shape[0] * k.shape[1]
+        p.block_table, p.block_table_stride = block_table.data_ptr(), block_table.stride(0)
+        p.k_stride_page, p.v_stride_page = k.stride(0), v.stride(0)
+        p.page_size, p.num_pages = k.shape[1], k.shape[0]
     p.batch = cu_q.numel() - 1
     p.n_heads, p.kv_heads, p.head_dim = n_heads, kv_heads, HEAD_DIM
     p.rel_extent = rel_extent
@@ -104,11 +129,19 @@ def _fill_common(p, q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent
 
 
 def _prepare(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, causal, window_size, n_heads,
-             kv_heads, head_dim, softmax_scale, causal_align, out):
+             kv_heads, head_dim, softmax_scale, causal_align, out, block_table=None):
     n_heads, kv_heads, rel_extent, window_left = _check_inputs(
         name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, n_heads, kv_heads, head_dim,
-        window_size, causal_align)
-    q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
+        window_size, causal_align, block_table)
+    if block_table is not None:
+        # a paged cache is never copied: it must already suit TMA
+        for nm, t in (("k", k), ("v", v)):
+            if _tma_ready(t) is not t:
+                raise ValueError(f"{name}: paged {nm} cache needs unit last stride, strides "
+                                 "that are positive multiples of 8 elements, 16-byte alignment")
+        q = _tma_ready(q)
+    else:
+        q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     rel = rel_logits if rel_logits.stride(-1) == 1 else rel_logits.contiguous()
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
@@ -123,19 +156,31 @@ def _prepare(name, q, k, v, rel_logits, cu_q, cu_k, rel_extent, causal, window_s
     return q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale
 
 
+def _table(block_table):
+    """Unit last stride, and never a NULL pointer (NULL means "not paged" in the C ABI): an empty
+    table becomes one column of -1 entries, which read as zero keys."""
+    if block_table is None or not isinstance(block_table, torch.Tensor):
+        return block_table
+    if block_table.dim() == 2 and block_table.numel() == 0 and block_table.shape[0] > 0:
+        return torch.full((block_table.shape[0], 1), -1, dtype=torch.int32,
+                          device=block_table.device)
+    return block_table if block_table.stride(-1) == 1 else block_table.contiguous()
+
+
 @torch.no_grad()
 def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
             rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
             head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
-            tile_config=0, return_lse=False, lse=None):
+            tile_config=0, return_lse=False, lse=None, block_table=None):
+    block_table = _table(block_table)
     q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
         "prefill", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
-        window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out)
+        window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out, block_table)
     lse = _lse_buffer(q, n_heads, return_lse, lse)
     p = _lib.PrefillParams()
     _fill_lse(p, lse)
     _fill_common(p, q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
-                 rel_extent, causal, window_left, causal_align)
+                 rel_extent, causal, window_left, causal_align, block_table)
     p.max_seqlen_q = int(max_seqlen_q) if max_seqlen_q else 0
     p.softmax_scale = scale
     p.tile_config = int(tile_config)
@@ -146,10 +191,11 @@ def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_s
 
 
 def _decode_params(q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
-                   window_left, causal_align, max_seqlen_k, scale, num_splits, chunk_len):
+                   window_left, causal_align, max_seqlen_k, scale, num_splits, chunk_len,
+                   block_table=None):
     p = _lib.DecodeParams()
     _fill_common(p, q, k, v, rel, out, cu_q, cu_k, n_heads, kv_heads, rel_extent, causal,
-                 window_left, causal_align)
+                 window_left, causal_align, block_table)
     p.max_seqlen_k = int(max_seqlen_k) if max_seqlen_k else 0
     p.softmax_scale = scale
     p.num_splits = int(num_splits)
@@ -171,10 +217,12 @@ def decode_plan(p) -> tuple[int, int, int]:
 def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
            rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
            head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
-           num_splits=0, chunk_len=0, workspace=None, return_lse=False, lse=None):
+           num_splits=0, chunk_len=0, workspace=None, return_lse=False, lse=None,
+           block_table=None):
+    block_table = _table(block_table)
     q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
         "decode", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
-        window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out)
+        window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out, block_table)
     lse = _lse_buffer(q, n_heads, return_lse, lse)
     if q.shape[0] != cu_seqlens_q.numel() - 1:
         raise ValueError("decode: expects exactly one query token per sequence")
@@ -182,7 +230,7 @@ def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_se
         q = q.contiguous()
     p = _decode_params(q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
                        rel_extent, causal, window_left, causal_align, max_seqlen_k, scale,
-                       num_splits, chunk_len)
+                       num_splits, chunk_len, block_table)
     _fill_lse(p, lse)
     with torch.cuda.device(q.device):
         nbytes, _, _ = decode_plan(p)

@@ -15,7 +15,7 @@ def inkling_fa4_rel_attention_triton(q, k, v, rel_logits, cu_seqlens_q, cu_seqle
                                      n_heads=None, kv_heads=None, head_dim=128,
                                      arch=None, *, softmax_scale=None,
                                      causal_align="reference", out=None, return_lse=False,
-                                     lse=None):
+                                     lse=None, block_table=None):
     """Relative-position-bias flash attention over packed variable-length sequences.
 
     Same arguments and meaning as the reference (triton_kernel.py:84-106):
@@ -35,12 +35,17 @@ def inkling_fa4_rel_attention_triton(q, k, v, rel_logits, cu_seqlens_q, cu_seqle
     ``return_lse=True`` (or an ``lse`` buffer) also returns the fp32 natural-log log-sum-exp of
     each row's scaled+biased logits, [n_heads, total_q] (-inf for rows with no visible key), for
     merging attention computed over separate key ranges.
+
+    ``block_table`` (int32 [batch, max_pages]) switches k / v to a paged KV cache
+    [num_pages, page_size, kv_heads, 128] (page_size a power of two >= 16): key j of sequence b
+    is slot j % page_size of page block_table[b, j // page_size]; cu_seqlens_k still gives the
+    key counts.  Cache slots past a sequence's last key are never used.
     """
     return _ops.prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
                         max_seqlen_k, rel_extent, causal=causal, window_size=window_size,
                         n_heads=n_heads, kv_heads=kv_heads, head_dim=head_dim,
                         softmax_scale=softmax_scale, causal_align=causal_align, out=out,
-                        return_lse=return_lse, lse=lse)
+                        return_lse=return_lse, lse=lse, block_table=block_table)
 
 
 __all__ = ["inkling_fa4_rel_attention_triton"]

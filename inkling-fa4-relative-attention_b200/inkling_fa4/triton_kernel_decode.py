@@ -17,7 +17,7 @@ def inkling_fa4_rel_attention_decode_triton(q, k, v, rel_logits, cu_seqlens_q, c
                                             arch=None, *, softmax_scale=None,
                                             causal_align="reference", out=None,
                                             num_splits=0, chunk_len=0, workspace=None,
-                                            return_lse=False, lse=None):
+                                            return_lse=False, lse=None, block_table=None):
     """Decode: q [batch, n_heads, 128] (one query per sequence, cu_seqlens_q = 0..batch),
     k/v [total_k, kv_heads, 128], rel_logits [batch, n_heads, >=rel_extent].
 
@@ -27,14 +27,15 @@ def inkling_fa4_rel_attention_decode_triton(q, k, v, rel_logits, cu_seqlens_q, c
     which the query is the last position of its sequence; "reference" reproduces the oracle,
     whose query sees key 0 only), ``out``, ``num_splits``/``chunk_len`` (0 = automatic) and a
     reusable ``workspace`` (uint8 CUDA tensor; allocated per call when absent), and
-    ``return_lse`` / ``lse`` as in the prefill entry point.
+    ``return_lse`` / ``lse`` and ``block_table`` (paged KV cache) as in the prefill entry
+    point.
     """
     return _ops.decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
                        max_seqlen_k, rel_extent, causal=causal, window_size=window_size,
                        n_heads=n_heads, kv_heads=kv_heads, head_dim=head_dim,
                        softmax_scale=softmax_scale, causal_align=causal_align, out=out,
                        num_splits=num_splits, chunk_len=chunk_len, workspace=workspace,
-                       return_lse=return_lse, lse=lse)
+                       return_lse=return_lse, lse=lse, block_table=block_table)
 
 
 __all__ = ["inkling_fa4_rel_attention_decode_triton"]

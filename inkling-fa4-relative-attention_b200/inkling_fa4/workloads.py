@@ -156,3 +156,42 @@ def causal_visible_pairs(seqlens_q, seqlens_k, causal=True, window_left=None,
                 for_all += hi - lo
         total += for_all
     return total
+
+
+def page_kv(case: Case, page_size: int = 16, seed: int = 0, spare_pages: int = 3,
+            extra_cols: int = 2, fill: float = float("nan")) -> Case:
+    """The same case with K/V moved into a paged cache, as a serving engine holds them:
+    caches [num_pages, page_size, kv_heads, d] whose pages are handed out in a seeded random
+    order, a block table [batch, max_pages + extra_cols] (int32, -1 past each sequence's pages),
+    and every slot that holds no key set to ``fill`` (NaN by default, so a kernel that let an
+    unused slot reach its output would show it).  cu_seqlens_k is unchanged (key counts)."""
+    lens = [int(x) for x in case.seqlens_k]
+    dev = case.k.device
+    n_per = [(n + page_size - 1) // page_size for n in lens]
+    used = sum(n_per)
+    num_pages = used + spare_pages
+    g = torch.Generator(device="cpu")
+    g.manual_seed(int(seed))
+    perm = torch.randperm(num_pages, generator=g)[:used].to(torch.int32)
+    max_pages = max(n_per) if n_per else 0
+    table = torch.full((len(lens), max_pages + extra_cols), -1, dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(n_per):
+        table[b, :n] = perm[off:off + n]
+        off += n
+    hkv, d = case.k.shape[1], case.k.shape[2]
+    kc = torch.full((num_pages, page_size, hkv, d), fill, dtype=case.k.dtype, device=dev)
+    vc = torch.full_like(kc, fill)
+    if sum(lens):
+        seq = torch.repeat_interleave(torch.arange(len(lens)), torch.tensor(lens))
+        starts = torch.tensor([0] + lens[:-1]).cumsum(0)
+        j = torch.arange(sum(lens)) - starts[seq]
+        page = table[seq, j // page_size].long().to(dev)
+        slot = (j % page_size).to(dev)
+        kc[page, slot] = case.k
+        vc[page, slot] = case.v
+    meta = dict(case.meta)
+    meta.update(block_table=table.to(dev), page_size=page_size, num_pages=num_pages)
+    return Case(q=case.q, k=kc, v=vc, rel=case.rel, cu_q=case.cu_q, cu_k=case.cu_k,
+                seqlens_q=case.seqlens_q, seqlens_k=case.seqlens_k, rel_extent=case.rel_extent,
+                meta=meta)

@@ -38,7 +38,11 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_tile_name():
     L = _lib.lib()
     assert L.ifa4_abi_version() == _lib.ABI_VERSION
-    assert L.ifa4_prefill_tile_config_name(0).startswith(b"sm100")
+    from inkling_fa4.autotune_configs import TILE_CONFIGS
+    names = [L.ifa4_prefill_tile_config_name(i) for i in range(len(TILE_CONFIGS))]
+    assert all(n is not None and n.startswith(b"sm100") for n in names), names
+    assert len(set(names)) == len(names)
+    assert L.ifa4_prefill_tile_config_name(len(TILE_CONFIGS)) == b""
     assert L.ifa4_prefill_tile_config_name(99) == b""
 
 
@@ -135,3 +139,54 @@ def test_decode_requires_workspace_when_split():
     p.chunk_len = 100
     assert L.ifa4_decode_workspace_size(ctypes.byref(p), ctypes.byref(nbytes), None,
                                         None) == _lib.IFA4_ERR_INVALID_ARGUMENT
+
+
+def _paged_params(**kw):
+    base = dict(q=16, k=16, v=16, rel=16, out=16, cu_seqlens_q=16, cu_seqlens_k=16,
+                q_stride_t=512, q_stride_h=128, k_stride_t=512, k_stride_h=128,
+                v_stride_t=512, v_stride_h=128, rel_stride_t=512, rel_stride_h=128,
+                out_stride_t=512, out_stride_h=128, block_table=16, block_table_stride=4,
+                page_size=16, num_pages=8, k_stride_page=16 * 512, v_stride_page=16 * 512)
+    base.update(kw)
+    return _params(**base)
+
+
+@pytest.mark.parametrize("kw,code,msg", [
+    (dict(page_size=8), _lib.IFA4_ERR_INVALID_ARGUMENT, b"page_size"),
+    (dict(page_size=48), _lib.IFA4_ERR_INVALID_ARGUMENT, b"page_size"),
+    (dict(num_pages=0), _lib.IFA4_ERR_INVALID_ARGUMENT, b"num_pages"),
+    (dict(block_table_stride=-1), _lib.IFA4_ERR_INVALID_ARGUMENT, b"block_table_stride"),
+    (dict(k_stride_page=4), _lib.IFA4_ERR_INVALID_ARGUMENT, b"page strides"),
+    (dict(v_stride_page=0), _lib.IFA4_ERR_INVALID_ARGUMENT, b"page strides"),
+    (dict(tile_config=2), _lib.IFA4_ERR_UNSUPPORTED, b"paged"),
+])
+def test_paged_cache_validation(kw, code, msg):
+    L = _lib.lib()
+    assert L.ifa4_prefill_launch(ctypes.byref(_paged_params(**kw)), None) == code
+    assert msg in L.ifa4_last_error_string()
+
+
+def test_page_kv_roundtrip():
+    """The paged test/bench layout holds exactly the contiguous keys, in shuffled pages, with
+    NaN in every unused slot and -1 past each sequence's pages."""
+    import numpy as np
+    from inkling_fa4.workloads import make_case, page_kv
+    lens = [0, 1, 15, 16, 17, 100]
+    c = make_case(lens, lens, 4, 2, 16, seed=4)
+    pc = page_kv(c, page_size=16, seed=9)
+    bt = pc.meta["block_table"]
+    cu = c.cu_k.tolist()
+    for b, n in enumerate(lens):
+        npg = (n + 15) // 16
+        assert bool((bt[b, npg:] == -1).all()) and bool((bt[b, :npg] >= 0).all())
+        for j in range(n):
+            pg, sl = int(bt[b, j // 16]), j % 16
+            assert torch.equal(pc.k[pg, sl], c.k[cu[b] + j]) and torch.equal(pc.v[pg, sl], c.v[cu[b] + j])
+    used = bt[bt >= 0]
+    assert len(set(used.tolist())) == used.numel()
+    mask = torch.zeros(pc.k.shape[:2], dtype=torch.bool)
+    for b, n in enumerate(lens):
+        for j in range(n):
+            mask[int(bt[b, j // 16]), j % 16] = True
+    assert bool(torch.isnan(pc.k[~mask].float()).all()) and bool(torch.isnan(pc.v[~mask].float()).all())
+    assert np.isfinite(pc.k[mask].float().numpy()).all()
