@@ -443,7 +443,8 @@ def main():
 
     # ---------------- ragged (config 2) and chunked (config 4) prefill, on request
     if args.extra_configs:
-        from inkling_fa4.workloads import causal_visible_pairs, config_chunked, config_ragged
+        from inkling_fa4.workloads import (causal_visible_pairs, config_chunked, config_ragged,
+                                           page_kv)
 
         for name, make, align in (("ragged", config_ragged, "reference"),
                                   ("chunked", config_chunked, "bottom_right")):
@@ -461,6 +462,21 @@ def main():
                             "unit": "TFLOP/s", "ms_per_step": xms / args.steps,
                             "flops_per_step_per_gpu": fl, "causal_align": align,
                             "seqlens_q": cc.seqlens_q if name == "ragged" else None}
+            if name == "chunked":  # the same chunks against a 16-token paged cache
+                pc = page_kv(cc, page_size=16, seed=rank)
+                del cc
+
+                def pstep(pc=pc):
+                    return inkling_fa4_rel_attention_triton(
+                        pc.q, pc.k, pc.v, pc.rel, pc.cu_q, pc.cu_k, pc.max_q, pc.max_k, R,
+                        causal_align="bottom_right", block_table=pc.meta["block_table"])
+
+                pms = timed(pstep, args.steps, args.warmup, stream, dist, barrier)
+                result["chunked_paged"] = {
+                    "value": world * fl * args.steps / (pms / 1e3) / 1e12, "unit": "TFLOP/s",
+                    "ms_per_step": pms / args.steps, "flops_per_step_per_gpu": fl,
+                    "page_size": 16, "num_pages": pc.meta["num_pages"]}
+                cc = pc
             del cc
         torch.cuda.empty_cache()
 
@@ -498,6 +514,25 @@ def main():
                          "traffic": (profile_traffic("decode_dram_traffic.md")
                                      if args.decode_batch == 128 else None)},
             "gpu_launches": args.steps * (2 if nsplit > 1 else 1)}
+        # the same step against a 16-token paged cache (pages handed out in random order)
+        from inkling_fa4.workloads import page_kv
+        pdc = page_kv(dc, page_size=16, seed=rank)
+        del dc
+        torch.cuda.empty_cache()
+
+        def paged_step():
+            return inkling_fa4_rel_attention_decode_triton(
+                pdc.q, pdc.k, pdc.v, pdc.rel, pdc.cu_q, pdc.cu_k, 1, max(lens), R,
+                causal_align="bottom_right", workspace=ws, block_table=pdc.meta["block_table"])
+
+        pms = timed(paged_step, args.steps, args.warmup, stream, dist, barrier)
+        pus = pms * 1e3 / args.steps
+        result["decode_paged"] = {
+            "value": world * dbytes * args.steps / (pms / 1e3) / 1e9, "unit": "GB/s",
+            "us_per_step": pus, "page_size": 16, "num_pages": pdc.meta["num_pages"],
+            "frac": dbytes / (pus / 1e6) / 1e9 / peaks["hbm_gbs"],
+            "bytes_per_step_per_gpu": dbytes + 4 * sum((n + 15) // 16 for n in lens)}
+        dc = pdc
         del dc, ws
         torch.cuda.empty_cache()
 
