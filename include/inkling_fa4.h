@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define IFA4_ABI_VERSION 3
+#define IFA4_ABI_VERSION 4
 
 enum {
   IFA4_OK = 0,
@@ -180,9 +180,67 @@ int ifa4_decode_workspace_size(const IFA4DecodeParams* params, size_t* bytes_out
  * the combine kernel reads it. */
 int ifa4_decode_launch_noalloc(const IFA4DecodeParams* params, void* stream);
 
+/* Backward of the prefill (varlen, causal / window, both alignments, GQA): gradients of the
+ * loss with respect to q, k, v and rel_logits given dout = dLoss/dout.  Not in the reference
+ * (it has no backward); the gradients are those of its forward, reference.py:4-39.
+ * out and lse are the forward's output and its log-sum-exp (IFA4PrefillParams.lse).
+ * dq [total_q, n_heads, 128], dk / dv [total_k, kv_heads, 128] are written in full (rows of
+ * keys no query sees get 0); drel [total_q, n_heads, >= rel_extent] has columns [0, rel_extent)
+ * written (the band gradient, 0 elsewhere) and later columns left untouched.  dout, dq, dk, dv
+ * and out follow q's layout rules (16-byte aligned, strides multiples of 8 elements); drel and
+ * lse need only a contiguous last dimension.  Deterministic: no atomics. */
+typedef struct IFA4BackwardParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* rel;
+  const void* out;
+  const void* dout;
+  const float* lse;
+  void* dq;
+  void* dk;
+  void* dv;
+  void* drel;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int64_t q_stride_t, q_stride_h;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  int64_t rel_stride_t, rel_stride_h;
+  int64_t out_stride_t, out_stride_h;
+  int64_t dout_stride_t, dout_stride_h;
+  int64_t lse_stride_h, lse_stride_t;
+  int64_t dq_stride_t, dq_stride_h;
+  int64_t dk_stride_t, dk_stride_h;
+  int64_t dv_stride_t, dv_stride_h;
+  int64_t drel_stride_t, drel_stride_h;
+  int64_t total_q;
+  int64_t total_k;
+  int32_t batch;
+  int32_t n_heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t rel_extent;
+  int32_t causal;
+  int32_t window_left;
+  int32_t causal_align;
+  int32_t max_seqlen_q;     /* grid-size hints, as in IFA4PrefillParams                 */
+  int32_t max_seqlen_k;
+  int32_t dtype;
+  float softmax_scale;
+} IFA4BackwardParams;
+
+/* Device workspace (bytes, 16-byte aligned) ifa4_backward_launch needs: fp32 row statistics. */
+int ifa4_backward_workspace_size(const IFA4BackwardParams* params, size_t* bytes_out);
+
+/* Backward.  Three kernels in order on `stream`: row statistics (and zeroing of the drel
+ * band), dK / dV / drel per key block, dQ per query tile. */
+int ifa4_backward_launch(const IFA4BackwardParams* params, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Reads (and optionally clears) the library's device status word on `stream`, blocking the
  * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on
- * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode.  Test hook; the
+ * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode, bit 2 backward.  Test hook; the
  * reference has no counterpart. */
 int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out);
 

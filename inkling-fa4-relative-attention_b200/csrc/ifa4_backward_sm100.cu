@@ -1,0 +1,883 @@
+// Backward pass of the relative-bias attention for sm_100a (B200): dQ, dK, dV and the gradient
+// of the relative logits.  The reference has no backward; the gradients are those of its
+// forward (reference.py:4-39) as torch autograd computes them through the oracle.
+//
+// With P = softmax(S * scale + bias) (masked), O = P V, L = logsumexp row statistic saved by the
+// forward (natural log) and dO the incoming gradient:
+//   Delta_i = sum_d dO_id O_id                        (prep kernel)
+//   dP = dO V^T,  dS = P o (dP - Delta)                (dS = gradient of the biased logits)
+//   dV = P^T dO,  dK = scale dS^T Q,  dQ = scale dS K,  d rel[i, h, d] = dS_ij for the key j at
+//   bias distance d = q_pos + bias_shift - k_pos (each (i, d) pair names one key, so the bias
+//   gradient is a scatter of dS along the band, without atomics).
+//
+// Three launches on the caller's stream:
+//   rel_attn_bwd_prep_kernel   Delta (fp32 workspace) and zeroes the band columns [0, R) of
+//                              d rel; one warp per (token, head).  HBM bound.
+//   rel_attn_bwd_dkdv_kernel   one CTA per (kv head, 128-key block): K and V stay in shared
+//                              memory while the Q and dO tiles of every query head of the GQA
+//                              group stream through a two-stage TMA ring.  The tensor core
+//                              computes S^T = K Q^T and dP^T = V dO^T into TMEM with the keys on
+//                              the 128 lanes, so P^T and dS^T are written back to TMEM as bf16
+//                              and feed dV += P^T dO and dK += dS^T Q directly (A operand from
+//                              TMEM, dO / Q as MN-major B operands): no shared-memory round
+//                              trip and both accumulators stay in TMEM (S^T | dP^T | dV | dK =
+//                              512 columns).  The d rel band is scattered from dS^T here.
+//   rel_attn_bwd_dq_kernel     one CTA per (query head, 128-row tile), shaped like the
+//                              forward: Q and dO stay in shared memory, K / V stream; S = Q K^T
+//                              is double-buffered in TMEM (S0 | S1 | dP | dQ) so the next tile's
+//                              QK^T overlaps this tile's elementwise work; dQ += dS K with dS
+//                              from TMEM.
+// dK / dV / dQ are written once per CTA (no atomics), so the backward is deterministic.
+//
+// Warp roles in both tensor-core kernels (384 threads): warp 0 TMA producer, warp 1 UMMA issuer
+// (one thread), warp 2 TMEM owner, warps 4-11 elementwise: warp w handles TMEM lanes
+// 32 (w % 4) .. +31 (one row each) and columns 64 ((w - 4) / 4) .. +63 of the 128-column tile.
+// There is no row reduction in the backward, so splitting columns between warps is free.
+// All waits are bounded (status word on timeout), as in the forward kernels.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ifa4_internal.h"
+#include "ifa4_ptx.cuh"
+
+namespace ifa4 {
+namespace bwd {
+
+constexpr int kBM = 128;  // query rows per tile
+constexpr int kBN = 128;  // keys per tile
+constexpr int kThreads = 384;
+constexpr uint32_t kHalf = 128u * 128u;  // 128 rows x 128 B (64 dims)
+constexpr uint32_t kTile = 2u * kHalf;   // 128 rows x 256 B (128 dims)
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kIdescKM = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
+constexpr uint32_t kIdescMN = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
+
+// D[128 x 128] = A B^T over 128 dims, A and B K-major 128-row tiles (two swizzled halves).
+__device__ __forceinline__ void mma_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
+  const uint64_t ad = sdesc_sw128(a_addr, 16, 1024);
+  const uint64_t bd = sdesc_sw128(b_addr, 16, 1024);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+    umma_ss(d_tmem, sdesc_advance(ad, off), sdesc_advance(bd, off), kIdescKM, kk > 0 ? 1u : 0u);
+  }
+}
+
+// D[128 x 128] (+)= A B with A in TMEM as bf16 (K = 128 split into two 64-wide halves stored
+// at column offsets 0 and 64 of a_tmem, 32 columns each) and B a 128-row MN-major tile (rows
+// = K, 128 dims = N).
+__device__ __forceinline__ void mma_tk(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr,
+                                       bool accumulate) {
+  const uint64_t bd = sdesc_sw128(b_addr, kHalf, 1024);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_ts(d_tmem, a_tmem + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_advance(bd, kk * 2048),
+            kIdescMN, (kk > 0 || accumulate) ? 1u : 0u);
+}
+
+__device__ __forceinline__ void store_row64_bf16(uint16_t* dst, const float* v, float mul) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * g + 0] * mul, v[8 * g + 1] * mul);
+    w.y = pack_bf16x2(v[8 * g + 2] * mul, v[8 * g + 3] * mul);
+    w.z = pack_bf16x2(v[8 * g + 4] * mul, v[8 * g + 5] * mul);
+    w.w = pack_bf16x2(v[8 * g + 6] * mul, v[8 * g + 7] * mul);
+    reinterpret_cast<uint4*>(dst)[g] = w;
+  }
+}
+
+__device__ __forceinline__ void store_zero_row64(uint16_t* dst) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) reinterpret_cast<uint4*>(dst)[g] = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// --------------------------------------------------------------------------------------
+// prep: Delta[h, t] = <dO[t, h], O[t, h]> and d rel[t, h, 0:R) = 0
+// --------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rel_attn_bwd_prep_kernel(const __grid_constant__
+                                                                    BackwardKernelArgs a) {
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= a.total_q * a.n_heads) return;
+  const long long t = row / a.n_heads;
+  const int h = static_cast<int>(row % a.n_heads);
+  const uint2 o = *reinterpret_cast<const uint2*>(a.out + t * a.out_st + h * a.out_sh + lane * 4);
+  const uint2 g = *reinterpret_cast<const uint2*>(a.dout + t * a.dout_st + h * a.dout_sh + lane * 4);
+  float acc = bf16_bits_to_float(o.x & 0xffffu) * bf16_bits_to_float(g.x & 0xffffu) +
+              bf16_bits_to_float(o.x >> 16) * bf16_bits_to_float(g.x >> 16) +
+              bf16_bits_to_float(o.y & 0xffffu) * bf16_bits_to_float(g.y & 0xffffu) +
+              bf16_bits_to_float(o.y >> 16) * bf16_bits_to_float(g.y >> 16);
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  if (lane == 0) a.delta[static_cast<long long>(h) * a.total_q + t] = acc;
+  uint16_t* dr = a.drel + t * a.drel_st + h * a.drel_sh;
+  for (int d = lane; d < a.rel_extent; d += 32) dr[d] = 0;
+}
+
+// --------------------------------------------------------------------------------------
+// dK / dV (and d rel)
+// --------------------------------------------------------------------------------------
+namespace kv {
+constexpr uint32_t kSmemK = 0;
+constexpr uint32_t kSmemV = kTile;
+constexpr uint32_t kSmemQ = 2 * kTile;   // 2 stages
+constexpr uint32_t kSmemDO = 4 * kTile;  // 2 stages
+constexpr uint32_t kSmemBar = 6 * kTile;
+// per elementwise warp: the lse (log2 domain) and Delta of its 64 query columns
+constexpr uint32_t kSmemVec = kSmemBar + 256;
+constexpr uint32_t kSmemBytes = kSmemVec + 8 * 128 * 4;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
+
+struct Bars {
+  uint64_t kv_full, kv_empty;
+  uint64_t qdo_full[2], qdo_empty[2];
+  uint64_t s_full, dp_full, p_full, ds_full;
+  uint64_t acc_full, acc_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+}  // namespace kv
+
+// Query tiles a key block [k0, k0 + 128) contributes to: [i_lo, i_lo + n_q) (per head).
+struct KeyBlock {
+  int i_lo, n_q;
+};
+
+__device__ __forceinline__ KeyBlock key_block(const BackwardKernelArgs& a, int k0, int sq, int sk) {
+  KeyBlock kb{0, 0};
+  const int ms = a.align_bottom_right ? sk - sq : 0;
+  const int k1 = min(k0 + kBN, sk);
+  int lo = 0, hi = sq;
+  if (a.causal) lo = max(0, k0 - ms);                         // q + ms >= k
+  if (a.window_left >= 0) hi = min(hi, k1 - 1 - ms + a.window_left + 1);  // q + ms - k <= W
+  if (k1 > k0 && hi > lo) {
+    kb.i_lo = lo / kBM;
+    kb.n_q = (hi + kBM - 1) / kBM - kb.i_lo;
+  }
+  return kb;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    rel_attn_bwd_dkdv_kernel(const __grid_constant__ BackwardKernelArgs a,
+                             const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v,
+                             const __grid_constant__ CUtensorMap tm_do) {
+  using namespace kv;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kSmemBar);
+  float* vec = reinterpret_cast<float*>(smem + kSmemVec);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x;
+  const int b = blockIdx.y;
+  const int group = a.n_heads / a.kv_heads;
+  const int q_start = a.cu_q[b];
+  const int sq = a.cu_q[b + 1] - q_start;
+  const int k_start = a.cu_k[b];
+  const int sk = a.cu_k[b + 1] - k_start;
+  const int n_kb = (sk + kBN - 1) / kBN;
+  if (static_cast<int>(blockIdx.z) >= n_kb) return;  // uniform over the CTA
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    mbar_init(&bars->kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->qdo_full[i], 1);
+      mbar_init(&bars->qdo_empty[i], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->p_full, 8);
+    mbar_init(&bars->ds_full, 8);
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 8);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_do);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  const AbortCtx ab{&bars->abort_flag, a.status, kStatusBackwardTimeout};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t ic = 0, sc = 0;
+      const uint64_t pol_kv = l2_policy_evict_first();
+      const uint64_t pol_q = l2_policy_evict_last();
+      bool ok = true;
+      for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
+        const KeyBlock blk = key_block(a, kb * kBN, sq, sk);
+        if (blk.n_q == 0) continue;
+        if (!(ok = mbar_wait(&bars->kv_empty, (ic & 1) ^ 1, ab))) break;
+        mbar_arrive_expect_tx(&bars->kv_full, 2 * kTile);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          tma_load_3d_hint(smem + kSmemK + hf * kHalf, &tm_k, &bars->kv_full, hf * 64, kvh,
+                           k_start + kb * kBN, pol_kv);
+          tma_load_3d_hint(smem + kSmemV + hf * kHalf, &tm_v, &bars->kv_full, hf * 64, kvh,
+                           k_start + kb * kBN, pol_kv);
+        }
+        ++ic;
+        for (int g = 0; g < group && ok; ++g) {
+          const int h = kvh * group + g;
+          for (int i = 0; i < blk.n_q; ++i, ++sc) {
+            const uint32_t st = sc & 1;
+            if (!(ok = mbar_wait(&bars->qdo_empty[st], ((sc >> 1) & 1) ^ 1, ab))) break;
+            mbar_arrive_expect_tx(&bars->qdo_full[st], 2 * kTile);
+            const int row = q_start + (blk.i_lo + i) * kBM;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              tma_load_3d_hint(smem + kSmemQ + st * kTile + hf * kHalf, &tm_q,
+                               &bars->qdo_full[st], hf * 64, h, row, pol_q);
+              tma_load_3d_hint(smem + kSmemDO + st * kTile + hf * kHalf, &tm_do,
+                               &bars->qdo_full[st], hf * 64, h, row, pol_q);
+            }
+          }
+        }
+      }
+      // drain: the loads of the last uses of every buffer have landed
+      if (ic > 0) mbar_wait(&bars->kv_full, (ic - 1) & 1, ab);
+      for (uint32_t i = 0; i < 2 && i < sc; ++i) {
+        const uint32_t last = sc - 1 - i;
+        mbar_wait(&bars->qdo_full[last & 1], (last >> 1) & 1, ab);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      uint32_t ic = 0, sc = 0;
+      const uint32_t k_addr = smem_u32(smem + kSmemK);
+      const uint32_t v_addr = smem_u32(smem + kSmemV);
+      const uint32_t q_addr = smem_u32(smem + kSmemQ);
+      const uint32_t do_addr = smem_u32(smem + kSmemDO);
+      bool ok = true;
+      for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
+        const KeyBlock blk = key_block(a, kb * kBN, sq, sk);
+        if (blk.n_q == 0) continue;
+        if (!(ok = mbar_wait(&bars->kv_full, ic & 1, ab))) break;
+        const int steps = group * blk.n_q;
+        for (int n = 0; n < steps; ++n, ++sc) {
+          const uint32_t st = sc & 1;
+          if (!(ok = mbar_wait(&bars->qdo_full[st], (sc >> 1) & 1, ab))) break;
+          tc_fence_after();
+          mma_kk(tbase + kColS, k_addr, q_addr + st * kTile);    // S^T = K Q^T
+          umma_commit(&bars->s_full);
+          mma_kk(tbase + kColDP, v_addr, do_addr + st * kTile);  // dP^T = V dO^T
+          umma_commit(&bars->dp_full);
+          if (n == 0 && !(ok = mbar_wait(&bars->acc_empty, (ic & 1) ^ 1, ab))) break;
+          if (!(ok = mbar_wait(&bars->p_full, sc & 1, ab))) break;
+          tc_fence_after();
+          mma_tk(tbase + kColDV, tbase + kColS, do_addr + st * kTile, n > 0);  // dV += P^T dO
+          if (!(ok = mbar_wait(&bars->ds_full, sc & 1, ab))) break;
+          tc_fence_after();
+          mma_tk(tbase + kColDK, tbase + kColDP, q_addr + st * kTile, n > 0);  // dK += dS^T Q
+          umma_commit(&bars->qdo_empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&bars->acc_full);
+        umma_commit(&bars->kv_empty);
+        ++ic;
+      }
+      umma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, ab);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ elementwise + epilogue
+    const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;        // columns [64 half, 64 half + 64)
+    const int r = quarter * 32 + lane;       // key row within the block
+    float* wvec = vec + (warp - 4) * 128;    // this warp's [lse2 64 | Delta 64]
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tbase + lane_off + kColS + half * 64;
+    const uint32_t t_dp = tbase + lane_off + kColDP + half * 64;
+    const int ms = a.align_bottom_right ? sk - sq : 0;
+    const int bs = a.align_bottom_right ? sk - sq : sq - sk;
+    uint32_t sc = 0, ec = 0;
+    bool ok = true;
+    for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
+      const int k0 = kb * kBN;
+      const KeyBlock blk = key_block(a, k0, sq, sk);
+      const int kl = k0 + r;  // this thread's key (local to the sequence)
+      const bool key_valid = kl < sk;
+      uint16_t* dk_row = a.dk + static_cast<long long>(k_start + kl) * a.dk_st +
+                         static_cast<long long>(kvh) * a.dk_sh + half * 64;
+      uint16_t* dv_row = a.dv + static_cast<long long>(k_start + kl) * a.dv_st +
+                         static_cast<long long>(kvh) * a.dv_sh + half * 64;
+      if (blk.n_q == 0) {  // no query sees these keys
+        if (key_valid) {
+          store_zero_row64(dk_row);
+          store_zero_row64(dv_row);
+        }
+        continue;
+      }
+      for (int g = 0; g < group && ok; ++g) {
+        const int h = kvh * group + g;
+        const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
+        uint16_t* drel_h = a.drel + static_cast<long long>(h) * a.drel_sh;
+        for (int i = 0; i < blk.n_q; ++i, ++sc) {
+          const int q0 = (blk.i_lo + i) * kBM;
+          // per-column statistics of this warp's 64 query columns: lse (log2 domain) and
+          // Delta, loaded by the warp itself (read back as broadcasts)
+          __syncwarp();  // the previous step's reads are done
+#pragma unroll
+          for (int i = lane; i < 128; i += 32) {
+            const int qq = q0 + half * 64 + (i & 63);
+            float v = 0.f;
+            if (qq < sq) {
+              const long long tok = q_start + qq;
+              v = i < 64 ? a.lse[static_cast<long long>(h) * a.lse_sh + tok * a.lse_st] * kLog2e
+                         : a.delta[static_cast<long long>(h) * a.total_q + tok];
+            }
+            wvec[i] = v;
+          }
+          __syncwarp();
+          const float* lse2 = wvec;
+          const float* dlt = wvec + 64;
+          // visible columns of this key: q in [c_lo, c_hi) relative to q0
+          int c_lo = a.causal ? kl - ms - q0 : -0x40000000;
+          int c_hi = sq - q0;
+          if (a.window_left >= 0) c_hi = min(c_hi, kl - ms + a.window_left - q0 + 1);
+          if (!key_valid) c_hi = -0x40000000;
+          const bool has_mask = c_lo > half * 64 || c_hi < half * 64 + 64;
+          // bias distance of column c (absolute 0..127): dq0 + c
+          const int dq0 = q0 + bs - kl;
+          const bool has_bias = key_valid && dq0 + half * 64 <= a.rel_extent - 1 &&
+                                dq0 + half * 64 + 63 >= 0;
+          if (!(ok = mbar_wait_warp(&bars->s_full, sc & 1, ab))) break;
+          tc_fence_after();
+          // P^T, 32 columns at a time; chunk c2's bf16 pairs go to columns [16 c2, 16 c2 + 16)
+          // of this half, which the chunks read so far already cover
+          float p[64];
+          const bool warp_bias = __any_sync(0xffffffffu, has_bias);
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t sr[32];
+            tmem_ld32(t_s + c2 * 32, sr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int c = c2 * 32 + i;
+              const int cq = half * 64 + c;
+              float bias = 0.f;
+              if (warp_bias) {
+                const int d = dq0 + cq;
+                if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
+                  bias = bf16_bits_to_float(
+                      __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
+              }
+              p[c] = fast_exp2(fmaf(__uint_as_float(sr[i]), a.scale_log2, bias * kLog2e - lse2[c]));
+              if (has_mask && (cq < c_lo || cq >= c_hi)) p[c] = 0.f;
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(p[c2 * 32 + 2 * i], p[c2 * 32 + 2 * i + 1]);
+            __syncwarp();
+            tmem_st16(t_s + c2 * 16, pk);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_full);
+          if (!(ok = mbar_wait_warp(&bars->dp_full, sc & 1, ab))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {  // dS^T, in place over dP^T as for P^T
+            uint32_t dr[32];
+            tmem_ld32(t_dp + c2 * 32, dr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              p[c2 * 32 + i] *= __uint_as_float(dr[i]) - dlt[c2 * 32 + i];
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(p[c2 * 32 + 2 * i], p[c2 * 32 + 2 * i + 1]);
+            __syncwarp();
+            tmem_st16(t_dp + c2 * 16, pk);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->ds_full);
+          // d rel: the band entries of this key (dS of masked pairs is 0)
+          if (warp_bias) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+              const int cq = half * 64 + c;
+              const int d = dq0 + cq;
+              if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0) {
+                __nv_bfloat16 v = __float2bfloat16_rn(p[c]);
+                drel_h[static_cast<long long>(q_start + q0 + cq) * a.drel_st + d] =
+                    *reinterpret_cast<uint16_t*>(&v);
+              }
+            }
+          }
+        }
+      }
+      if (!ok) break;
+      // epilogue: dV and scale * dK of this thread's key row, half of the columns
+      if (!(ok = mbar_wait_warp(&bars->acc_full, ec & 1, ab))) break;
+      ++ec;
+      tc_fence_after();
+      {
+        uint32_t v0[32], v1[32];
+        float f[64];
+        tmem_ld32(tbase + lane_off + kColDV + half * 64, v0);
+        tmem_ld32(tbase + lane_off + kColDV + half * 64 + 32, v1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          f[c] = __uint_as_float(v0[c]);
+          f[32 + c] = __uint_as_float(v1[c]);
+        }
+        if (key_valid) store_row64_bf16(dv_row, f, 1.f);
+        tmem_ld32(tbase + lane_off + kColDK + half * 64, v0);
+        tmem_ld32(tbase + lane_off + kColDK + half * 64 + 32, v1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          f[c] = __uint_as_float(v0[c]);
+          f[32 + c] = __uint_as_float(v1[c]);
+        }
+        if (key_valid) store_row64_bf16(dk_row, f, a.scale);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------------------------
+// dQ
+// --------------------------------------------------------------------------------------
+namespace q {
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemDO = kTile;
+constexpr uint32_t kSmemK = 2 * kTile;  // 2 stages
+constexpr uint32_t kSmemV = 4 * kTile;  // 2 stages
+constexpr uint32_t kSmemBar = 6 * kTile;
+// per elementwise warp, a 32-row x 32-column bf16 transpose buffer for the bias gather (rows
+// 34 halfwords apart: conflict-free row writes and per-lane row reads)
+constexpr uint32_t kBiasRowHalves = 34;
+constexpr uint32_t kBiasWarpBytes = 32 * kBiasRowHalves * 2;
+constexpr uint32_t kSmemBias = kSmemBar + 256;
+constexpr uint32_t kSmemBytes = kSmemBias + 8 * kBiasWarpBytes;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
+constexpr uint32_t kColS = 0, kColDP = 256, kColDQ = 384;  // S0 | S1 | dP | dQ
+
+struct Bars {
+  uint64_t qdo_full, qdo_empty;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];
+  uint64_t dp_full, ds_full;
+  uint64_t acc_full, acc_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+}  // namespace q
+
+struct QTile {
+  int j_lo, n_kv;
+};
+
+__device__ __forceinline__ QTile q_tile(const BackwardKernelArgs& a, int q0, int sq, int sk) {
+  QTile t{0, 0};
+  const int ms = a.align_bottom_right ? sk - sq : 0;
+  const int r1 = min(q0 + kBM, sq);
+  int hi = sk;
+  if (a.causal) hi = min(hi, r1 + ms);
+  int lo = 0;
+  if (a.window_left >= 0) lo = max(0, q0 + ms - a.window_left);
+  if (r1 > q0 && hi > lo) {
+    t.j_lo = lo / kBN;
+    t.n_kv = (hi + kBN - 1) / kBN - t.j_lo;
+  }
+  return t;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    rel_attn_bwd_dq_kernel(const __grid_constant__ BackwardKernelArgs a,
+                           const __grid_constant__ CUtensorMap tm_q,
+                           const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v,
+                           const __grid_constant__ CUtensorMap tm_do) {
+  using namespace q;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kSmemBar);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int b = blockIdx.y;
+  const int kvh = h / (a.n_heads / a.kv_heads);
+  const int q_start = a.cu_q[b];
+  const int sq = a.cu_q[b + 1] - q_start;
+  const int k_start = a.cu_k[b];
+  const int sk = a.cu_k[b + 1] - k_start;
+  const int n_qt = (sq + kBM - 1) / kBM;
+  if (static_cast<int>(blockIdx.z) >= n_qt) return;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->qdo_full, 1);
+    mbar_init(&bars->qdo_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+    }
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->ds_full, 8);
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 8);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_do);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  const AbortCtx ab{&bars->abort_flag, a.status, kStatusBackwardTimeout};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t qc = 0, kc = 0, vc = 0;
+      const uint64_t pol_kv = l2_policy_evict_last();
+      const uint64_t pol_q = l2_policy_evict_first();
+      bool ok = true;
+      for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+        const int q0 = (n_qt - 1 - slot) * kBM;
+        const QTile t = q_tile(a, q0, sq, sk);
+        if (t.n_kv == 0) continue;
+        if (!(ok = mbar_wait(&bars->qdo_empty, (qc & 1) ^ 1, ab))) break;
+        mbar_arrive_expect_tx(&bars->qdo_full, 2 * kTile);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          tma_load_3d_hint(smem + kSmemQ + hf * kHalf, &tm_q, &bars->qdo_full, hf * 64, h,
+                           q_start + q0, pol_q);
+          tma_load_3d_hint(smem + kSmemDO + hf * kHalf, &tm_do, &bars->qdo_full, hf * 64, h,
+                           q_start + q0, pol_q);
+        }
+        ++qc;
+        for (int j = 0; j < t.n_kv && ok; ++j) {
+          const int row = k_start + (t.j_lo + j) * kBN;
+          const uint32_t ks = kc & 1;
+          if (!(ok = mbar_wait(&bars->k_empty[ks], ((kc >> 1) & 1) ^ 1, ab))) break;
+          mbar_arrive_expect_tx(&bars->k_full[ks], kTile);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d_hint(smem + kSmemK + ks * kTile + hf * kHalf, &tm_k, &bars->k_full[ks],
+                             hf * 64, kvh, row, pol_kv);
+          ++kc;
+          const uint32_t vs = vc & 1;
+          if (!(ok = mbar_wait(&bars->v_empty[vs], ((vc >> 1) & 1) ^ 1, ab))) break;
+          mbar_arrive_expect_tx(&bars->v_full[vs], kTile);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d_hint(smem + kSmemV + vs * kTile + hf * kHalf, &tm_v, &bars->v_full[vs],
+                             hf * 64, kvh, row, pol_kv);
+          ++vc;
+        }
+      }
+      if (qc > 0) mbar_wait(&bars->qdo_full, (qc - 1) & 1, ab);
+      for (uint32_t i = 0; i < 2 && i < kc; ++i) {
+        const uint32_t last = kc - 1 - i;
+        mbar_wait(&bars->k_full[last & 1], (last >> 1) & 1, ab);
+      }
+      for (uint32_t i = 0; i < 2 && i < vc; ++i) {
+        const uint32_t last = vc - 1 - i;
+        mbar_wait(&bars->v_full[last & 1], (last >> 1) & 1, ab);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      uint32_t qc = 0, kc = 0, vc = 0, sc = 0, ec = 0;
+      const uint32_t q_addr = smem_u32(smem + kSmemQ);
+      const uint32_t do_addr = smem_u32(smem + kSmemDO);
+      const uint32_t k_addr = smem_u32(smem + kSmemK);
+      const uint32_t v_addr = smem_u32(smem + kSmemV);
+      bool ok = true;
+      for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+        const int q0 = (n_qt - 1 - slot) * kBM;
+        const QTile t = q_tile(a, q0, sq, sk);
+        if (t.n_kv == 0) continue;
+        if (!(ok = mbar_wait(&bars->qdo_full, qc & 1, ab))) break;
+        ++qc;
+        // first tile: S_0 = Q K_0^T, dP_0 = dO V_0^T
+        if (!(ok = mbar_wait(&bars->k_full[kc & 1], (kc >> 1) & 1, ab))) break;
+        tc_fence_after();
+        mma_kk(tbase + kColS + (sc & 1) * 128, q_addr, k_addr + (kc & 1) * kTile);
+        umma_commit(&bars->s_full[sc & 1]);
+        if (!(ok = mbar_wait(&bars->v_full[vc & 1], (vc >> 1) & 1, ab))) break;
+        tc_fence_after();
+        mma_kk(tbase + kColDP, do_addr, v_addr + (vc & 1) * kTile);
+        umma_commit(&bars->dp_full);
+        for (int j = 0; j < t.n_kv && ok; ++j) {
+          const uint32_t ks = kc & 1, vs = vc & 1;
+          if (j + 1 < t.n_kv) {  // next tile's S into the other buffer, overlapping this dS
+            const uint32_t kn = kc + 1;
+            if (!(ok = mbar_wait(&bars->k_full[kn & 1], (kn >> 1) & 1, ab))) break;
+            tc_fence_after();
+            mma_kk(tbase + kColS + ((sc + 1) & 1) * 128, q_addr, k_addr + (kn & 1) * kTile);
+            umma_commit(&bars->s_full[(sc + 1) & 1]);
+          }
+          if (j == 0 && !(ok = mbar_wait(&bars->acc_empty, (ec & 1) ^ 1, ab))) break;
+          if (!(ok = mbar_wait(&bars->ds_full, sc & 1, ab))) break;
+          tc_fence_after();
+          mma_tk(tbase + kColDQ, tbase + kColS + (sc & 1) * 128, k_addr + ks * kTile, j > 0);
+          umma_commit(&bars->k_empty[ks]);
+          umma_commit(&bars->v_empty[vs]);
+          ++kc;
+          ++vc;
+          ++sc;
+          if (j + 1 < t.n_kv) {
+            if (!(ok = mbar_wait(&bars->v_full[vc & 1], (vc >> 1) & 1, ab))) break;
+            tc_fence_after();
+            mma_kk(tbase + kColDP, do_addr, v_addr + (vc & 1) * kTile);
+            umma_commit(&bars->dp_full);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&bars->acc_full);
+        umma_commit(&bars->qdo_empty);
+        ++ec;
+      }
+      umma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, ab);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ elementwise + epilogue
+    const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int ms = a.align_bottom_right ? sk - sq : 0;
+    const int bs = a.align_bottom_right ? sk - sq : sq - sk;
+    uint16_t* bias_buf = reinterpret_cast<uint16_t*>(smem + kSmemBias + (warp - 4) * kBiasWarpBytes);
+    uint32_t sc = 0, ec = 0;
+    bool ok = true;
+    for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+      const int q0 = (n_qt - 1 - slot) * kBM;
+      const QTile t = q_tile(a, q0, sq, sk);
+      const int qi = q0 + r;
+      const bool row_valid = qi < sq;
+      uint16_t* dq_row = a.dq + static_cast<long long>(q_start + qi) * a.dq_st +
+                         static_cast<long long>(h) * a.dq_sh + half * 64;
+      if (t.n_kv == 0) {
+        if (row_valid) store_zero_row64(dq_row);
+        continue;
+      }
+      float lse2 = 0.f, dlt = 0.f;
+      if (row_valid) {
+        const long long tok = q_start + qi;
+        lse2 = a.lse[static_cast<long long>(h) * a.lse_sh + tok * a.lse_st] * kLog2e;
+        dlt = a.delta[static_cast<long long>(h) * a.total_q + tok];
+      }
+      const uint16_t* rel_row = a.rel + static_cast<long long>(q_start + qi) * a.rel_st +
+                                static_cast<long long>(h) * a.rel_sh;
+      int key_hi = sk;
+      if (a.causal) key_hi = min(key_hi, qi + ms + 1);
+      int key_lo = a.window_left >= 0 ? max(0, qi + ms - a.window_left) : 0;
+      if (!row_valid) key_hi = key_lo = 0;
+      const int dmax = qi + bs;  // bias distance at key 0
+      for (int j = 0; j < t.n_kv; ++j, ++sc) {
+        const int k0 = (t.j_lo + j) * kBN;
+        const uint32_t t_s = tbase + lane_off + kColS + (sc & 1) * 128 + half * 64;
+        const int cb = half * 64;                       // first column of this half
+        const int cl = key_lo - k0, ch = key_hi - k0;   // visible columns [cl, ch)
+        const bool has_mask = cl > cb || ch < cb + 64;
+        const int bl = dmax - a.rel_extent + 1 - k0;    // first column with bias
+        const int bh = dmax - k0;                       // last column with bias
+        const bool has_bias = row_valid && bl <= cb + 63 && bh >= cb;
+        if (!(ok = mbar_wait_warp(&bars->s_full[sc & 1], (sc >> 1) & 1, ab))) break;
+        tc_fence_after();
+        float p[64];
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t sr[32];
+          tmem_ld32(t_s + c2 * 32, sr);
+          tmem_wait_ld();
+          float x[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(sr[i]) * a.scale_log2 - lse2;
+          const int c0 = cb + c2 * 32;  // absolute first column of this chunk
+          const bool chunk_bias = has_bias && c0 + 31 >= bl && c0 <= bh;
+          if (__any_sync(0xffffffffu, chunk_bias)) {
+            // the warp gathers its 32 rows' bias for these 32 columns (coalesced row reads),
+            // transposes through shared memory, and each lane adds its own row
+            uint16_t v[32];
+#pragma unroll
+            for (int tr = 0; tr < 32; ++tr) {
+              const int qi_t = qi - lane + tr;
+              const int d = qi_t + bs - k0 - (c0 + lane);
+              v[tr] = 0;
+              if (qi_t < sq && d >= 0 && d < a.rel_extent)
+                v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
+            }
+#pragma unroll
+            for (int tr = 0; tr < 32; ++tr) bias_buf[tr * kBiasRowHalves + lane] = v[tr];
+            __syncwarp();
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(bias_buf) + lane * (kBiasRowHalves / 2);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const uint32_t pr = w[k];
+              x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
+              x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
+            }
+            __syncwarp();
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) p[c2 * 32 + i] = fast_exp2(x[i]);
+          if (has_mask) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = c0 + i;
+              if (col < cl || col >= ch) p[c2 * 32 + i] = 0.f;
+            }
+          }
+        }
+        if (!(ok = mbar_wait_warp(&bars->dp_full, sc & 1, ab))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {  // dS over this half's first 32 columns of the S buffer
+          uint32_t dr[32];
+          tmem_ld32(tbase + lane_off + kColDP + half * 64 + c2 * 32, dr);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(p[c2 * 32 + 2 * i] * (__uint_as_float(dr[2 * i]) - dlt),
+                                p[c2 * 32 + 2 * i + 1] * (__uint_as_float(dr[2 * i + 1]) - dlt));
+          __syncwarp();
+          tmem_st16(t_s + c2 * 16, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_full);
+      }
+      if (!ok) break;
+      if (!(ok = mbar_wait_warp(&bars->acc_full, ec & 1, ab))) break;
+      ++ec;
+      tc_fence_after();
+      {
+        uint32_t v0[32], v1[32];
+        float f[64];
+        tmem_ld32(tbase + lane_off + kColDQ + half * 64, v0);
+        tmem_ld32(tbase + lane_off + kColDQ + half * 64 + 32, v1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          f[c] = __uint_as_float(v0[c]);
+          f[32 + c] = __uint_as_float(v1[c]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty);
+        if (row_valid) store_row64_bf16(dq_row, f, a.scale);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+}  // namespace bwd
+
+namespace {
+template <class K>
+cudaError_t set_smem(K kernel, uint32_t bytes, bool* done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bytes));
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t launch_backward_sm100(const BackwardKernelArgs& args, const CUtensorMap& tm_q,
+                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                  const CUtensorMap& tm_do, int q_slots, int k_slots,
+                                  cudaStream_t stream) {
+  static bool kv_attr[64] = {false}, q_attr[64] = {false};
+  cudaError_t e = set_smem(bwd::rel_attn_bwd_dkdv_kernel, bwd::kv::kSmemAlloc, kv_attr);
+  if (e != cudaSuccess) return e;
+  e = set_smem(bwd::rel_attn_bwd_dq_kernel, bwd::q::kSmemAlloc, q_attr);
+  if (e != cudaSuccess) return e;
+  const long long rows = args.total_q * args.n_heads;
+  if (rows > 0) {
+    const long long blocks = (rows + 7) / 8;
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+    bwd::rel_attn_bwd_prep_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(args);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  dim3 kgrid(args.kv_heads, args.batch, k_slots);
+  bwd::rel_attn_bwd_dkdv_kernel<<<kgrid, bwd::kThreads, bwd::kv::kSmemAlloc, stream>>>(
+      args, tm_q, tm_k, tm_v, tm_do);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dim3 qgrid(args.n_heads, args.batch, q_slots);
+  bwd::rel_attn_bwd_dq_kernel<<<qgrid, bwd::kThreads, bwd::q::kSmemAlloc, stream>>>(
+      args, tm_q, tm_k, tm_v, tm_do);
+  return cudaGetLastError();
+}
+
+}  // namespace ifa4

@@ -501,6 +501,154 @@ int ifa4_decode_launch_noalloc(const IFA4DecodeParams* p, void* stream) {
                             stream);
 }
 
+// ---------------------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+int validate_backward(const IFA4BackwardParams* p) {
+  if (p == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: params is NULL");
+  if (p->dtype != IFA4_DTYPE_BF16)
+    return fail(IFA4_ERR_UNSUPPORTED, "backward: dtype %d unsupported (bf16 only)", p->dtype);
+  if (p->head_dim != ifa4::kHeadDim)
+    return fail(IFA4_ERR_UNSUPPORTED, "backward: head_dim %d unsupported (128 only)", p->head_dim);
+  if (p->batch < 0 || p->total_q < 0 || p->total_k < 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: negative batch/total");
+  if (p->n_heads <= 0 || p->kv_heads <= 0 || p->n_heads % p->kv_heads != 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT,
+                "backward: n_heads %d must be a positive multiple of kv_heads %d", p->n_heads,
+                p->kv_heads);
+  if (p->rel_extent <= 0) return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: rel_extent must be > 0");
+  if (!(p->softmax_scale > 0.f))
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: softmax_scale must be > 0");
+  if (p->causal_align != IFA4_ALIGN_REFERENCE && p->causal_align != IFA4_ALIGN_BOTTOM_RIGHT)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: causal_align %d", p->causal_align);
+  if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
+  if (!p->q || !p->k || !p->v || !p->rel || !p->out || !p->dout || !p->lse || !p->dq ||
+      !p->dk || !p->dv || !p->drel || !p->cu_seqlens_q || !p->cu_seqlens_k)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: null tensor pointer");
+  const void* a16[] = {p->q, p->k, p->v, p->out, p->dout, p->dq, p->dk, p->dv};
+  for (const void* ptr : a16)
+    if (!aligned16(ptr))
+      return fail(IFA4_ERR_INVALID_ARGUMENT,
+                  "backward: q/k/v/out/dout/dq/dk/dv must be 16-byte aligned");
+  const int64_t s8[] = {p->q_stride_t,    p->q_stride_h,  p->k_stride_t,  p->k_stride_h,
+                        p->v_stride_t,    p->v_stride_h,  p->out_stride_t, p->out_stride_h,
+                        p->dout_stride_t, p->dout_stride_h, p->dq_stride_t, p->dq_stride_h,
+                        p->dk_stride_t,   p->dk_stride_h, p->dv_stride_t,  p->dv_stride_h};
+  for (int64_t s : s8)
+    if (s <= 0 || (s % 8) != 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT,
+                  "backward: q/k/v/out/dout/dq/dk/dv token and head strides must be positive "
+                  "multiples of 8 elements");
+  if (p->rel_stride_t < 0 || p->rel_stride_h < 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: negative rel strides");
+  if (p->drel_stride_t <= 0 || p->drel_stride_h <= 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: drel strides must be positive");
+  if (p->batch > 65535) return fail(IFA4_ERR_UNSUPPORTED, "backward: batch > 65535");
+  return IFA4_OK;
+}
+
+size_t backward_workspace_bytes(const IFA4BackwardParams* p) {
+  return static_cast<size_t>(p->n_heads) * static_cast<size_t>(p->total_q) * sizeof(float);
+}
+}  // namespace
+
+extern "C" {
+
+int ifa4_backward_workspace_size(const IFA4BackwardParams* p, size_t* bytes_out) {
+  g_last_error[0] = '\0';
+  int rc = validate_backward(p);
+  if (rc) return rc;
+  if (bytes_out == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: bytes_out is NULL");
+  *bytes_out = (p->batch == 0 || p->total_q == 0) ? 0 : backward_workspace_bytes(p);
+  return IFA4_OK;
+}
+
+int ifa4_backward_launch(const IFA4BackwardParams* p, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  g_last_error[0] = '\0';
+  int rc = validate_backward(p);
+  if (rc) return rc;
+  if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
+  const size_t ws = backward_workspace_bytes(p);
+  if (workspace == nullptr || workspace_bytes < ws)
+    return fail(IFA4_ERR_WORKSPACE, "backward: workspace of %zu bytes required, got %zu", ws,
+                workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+    return fail(IFA4_ERR_WORKSPACE, "backward: workspace must be 16-byte aligned");
+  int* status = nullptr;
+  if ((rc = device_status_ptr(&status))) return rc;
+
+  ifa4::BackwardKernelArgs a{};
+  a.rel = static_cast<const uint16_t*>(p->rel);
+  a.out = static_cast<const uint16_t*>(p->out);
+  a.dout = static_cast<const uint16_t*>(p->dout);
+  a.lse = p->lse;
+  a.delta = static_cast<float*>(workspace);
+  a.dq = static_cast<uint16_t*>(p->dq);
+  a.dk = static_cast<uint16_t*>(p->dk);
+  a.dv = static_cast<uint16_t*>(p->dv);
+  a.drel = static_cast<uint16_t*>(p->drel);
+  a.cu_q = p->cu_seqlens_q;
+  a.cu_k = p->cu_seqlens_k;
+  a.rel_st = p->rel_stride_t;
+  a.rel_sh = p->rel_stride_h;
+  a.out_st = p->out_stride_t;
+  a.out_sh = p->out_stride_h;
+  a.dout_st = p->dout_stride_t;
+  a.dout_sh = p->dout_stride_h;
+  a.lse_sh = p->lse_stride_h;
+  a.lse_st = p->lse_stride_t;
+  a.dq_st = p->dq_stride_t;
+  a.dq_sh = p->dq_stride_h;
+  a.dk_st = p->dk_stride_t;
+  a.dk_sh = p->dk_stride_h;
+  a.dv_st = p->dv_stride_t;
+  a.dv_sh = p->dv_stride_h;
+  a.drel_st = p->drel_stride_t;
+  a.drel_sh = p->drel_stride_h;
+  a.total_q = p->total_q;
+  a.batch = p->batch;
+  a.n_heads = p->n_heads;
+  a.kv_heads = p->kv_heads;
+  a.rel_extent = p->rel_extent;
+  a.causal = p->causal ? 1 : 0;
+  a.window_left = p->window_left < 0 ? -1 : p->window_left;
+  a.align_bottom_right = p->causal_align == IFA4_ALIGN_BOTTOM_RIGHT;
+  a.scale = p->softmax_scale;
+  a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  a.status = status;
+
+  CUtensorMap tq, tk, tv, tdo;
+  const int64_t krows = p->total_k > 0 ? p->total_k : 1;
+  if ((rc = encode_rows_heads_dims(&tq, p->q, p->total_q, p->n_heads, p->q_stride_t,
+                                   p->q_stride_h, 128, "q")))
+    return rc;
+  if ((rc = encode_rows_heads_dims(&tdo, p->dout, p->total_q, p->n_heads, p->dout_stride_t,
+                                   p->dout_stride_h, 128, "dout")))
+    return rc;
+  if ((rc = encode_rows_heads_dims(&tk, p->k, krows, p->kv_heads, p->k_stride_t, p->k_stride_h,
+                                   128, "k")))
+    return rc;
+  if ((rc = encode_rows_heads_dims(&tv, p->v, krows, p->kv_heads, p->v_stride_t, p->v_stride_h,
+                                   128, "v")))
+    return rc;
+  int64_t max_sq = p->max_seqlen_q > 0 ? p->max_seqlen_q : p->total_q;
+  if (max_sq > p->total_q) max_sq = p->total_q;
+  int64_t max_sk = p->max_seqlen_k > 0 ? p->max_seqlen_k : p->total_k;
+  if (max_sk > p->total_k) max_sk = p->total_k;
+  int64_t qs = (max_sq + 127) / 128, ks = (max_sk + 127) / 128;
+  qs = qs < 1 ? 1 : (qs > 65535 ? 65535 : qs);
+  ks = ks < 1 ? 1 : (ks > 65535 ? 65535 : ks);
+  cudaError_t e = ifa4::launch_backward_sm100(a, tq, tk, tv, tdo, static_cast<int>(qs),
+                                              static_cast<int>(ks),
+                                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+  return IFA4_OK;
+}
+
 int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out) {
   g_last_error[0] = '\0';
   if (status_out == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "status_out is NULL");

@@ -12,6 +12,7 @@ constexpr int kHeadDim = 128;
 // Status bits written by kernels that abandoned a bounded wait.
 constexpr int kStatusPrefillTimeout = 1;
 constexpr int kStatusDecodeTimeout = 2;
+constexpr int kStatusBackwardTimeout = 4;
 
 struct PrefillKernelArgs {
   const uint16_t* rel;       // bf16 bits
@@ -88,5 +89,33 @@ struct DecodeKernelArgs {
 
 cudaError_t launch_decode_sm100(const DecodeKernelArgs& args, const CUtensorMap& tm_k,
                                 const CUtensorMap& tm_v, cudaStream_t stream);
+
+struct BackwardKernelArgs {
+  const uint16_t* rel;       // bf16 bits
+  const uint16_t* out;       // forward output O
+  const uint16_t* dout;      // incoming gradient dO
+  const float* lse;          // forward natural-log LSE, [h * lse_sh + token * lse_st]
+  float* delta;              // workspace [n_heads, total_q]: rowsum(dO * O)
+  uint16_t* dq;
+  uint16_t* dk;
+  uint16_t* dv;
+  uint16_t* drel;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  long long rel_st, rel_sh, out_st, out_sh, dout_st, dout_sh, lse_sh, lse_st;
+  long long dq_st, dq_sh, dk_st, dk_sh, dv_st, dv_sh, drel_st, drel_sh;
+  long long total_q;
+  int batch, n_heads, kv_heads, rel_extent;
+  int causal, window_left, align_bottom_right;
+  float scale;               // softmax_scale
+  float scale_log2;          // softmax_scale * log2(e)
+  int* status;
+};
+
+// Prep (Delta, zeroed d rel band), dK/dV (+ d rel) and dQ kernels, in that order on `stream`.
+cudaError_t launch_backward_sm100(const BackwardKernelArgs& args, const CUtensorMap& tm_q,
+                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                  const CUtensorMap& tm_do, int q_slots, int k_slots,
+                                  cudaStream_t stream);
 
 }  // namespace ifa4

@@ -19,7 +19,7 @@ IFA4_ERR_DEVICE_TIMEOUT = -5
 IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0
-ABI_VERSION = 3
+ABI_VERSION = 4
 NOALLOC_DECODE_SCRATCH_BYTES = 16 * 1024 * 1024
 
 EXPORTED_SYMBOLS = (
@@ -27,6 +27,8 @@ EXPORTED_SYMBOLS = (
     "ifa4_decode_launch",
     "ifa4_decode_launch_noalloc",
     "ifa4_decode_workspace_size",
+    "ifa4_backward_launch",
+    "ifa4_backward_workspace_size",
     "ifa4_read_device_status",
     "ifa4_prefill_tile_config_name",
     "ifa4_last_error_string",
@@ -74,6 +76,25 @@ class DecodeParams(ctypes.Structure):
     ]
 
 
+def _pairs(*names):
+    return [(f"{n}_stride_{x}", ctypes.c_int64) for n in names for x in ("t", "h")]
+
+
+class BackwardParams(ctypes.Structure):
+    """Mirror of ``IFA4BackwardParams``."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("q", "k", "v", "rel", "out", "dout", "lse", "dq",
+                                               "dk", "dv", "drel", "cu_seqlens_q",
+                                               "cu_seqlens_k")] + \
+        _pairs("q", "k", "v", "rel", "out", "dout") + \
+        [("lse_stride_h", ctypes.c_int64), ("lse_stride_t", ctypes.c_int64)] + \
+        _pairs("dq", "dk", "dv", "drel") + \
+        [("total_q", ctypes.c_int64), ("total_k", ctypes.c_int64)] + \
+        [(n, ctypes.c_int32) for n in ("batch", "n_heads", "kv_heads", "head_dim", "rel_extent",
+                                       "causal", "window_left", "causal_align", "max_seqlen_q",
+                                       "max_seqlen_k", "dtype")] + \
+        [("softmax_scale", ctypes.c_float)]
+
+
 class Ifa4Error(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"inkling_fa4 error {code}: {message}")
@@ -103,6 +124,10 @@ def lib() -> ctypes.CDLL:
     L.ifa4_decode_workspace_size.argtypes = [ctypes.POINTER(DecodeParams), ctypes.POINTER(sz),
                                              ctypes.POINTER(i32), ctypes.POINTER(i32)]
     L.ifa4_decode_workspace_size.restype = ctypes.c_int
+    L.ifa4_backward_launch.argtypes = [ctypes.POINTER(BackwardParams), vp, sz, vp]
+    L.ifa4_backward_launch.restype = ctypes.c_int
+    L.ifa4_backward_workspace_size.argtypes = [ctypes.POINTER(BackwardParams), ctypes.POINTER(sz)]
+    L.ifa4_backward_workspace_size.restype = ctypes.c_int
     L.ifa4_read_device_status.argtypes = [vp, i32, ctypes.POINTER(i32)]
     L.ifa4_read_device_status.restype = ctypes.c_int
     L.ifa4_prefill_tile_config_name.argtypes = [i32]

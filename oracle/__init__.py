@@ -8,4 +8,5 @@ from .rel_attn_oracle import (  # noqa: F401
     alignment_offsets,
     rel_attn_torch,
     rel_attn_rows_torch,
+    rel_attn_grads_torch,
 )

@@ -221,3 +221,23 @@ def rel_attn_torch(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, scale, rel_e
                     torch.arange(r0, r1), sq, sk, scale, rel_extent, causal, window_left,
                     causal_align)
     return out
+
+
+def rel_attn_grads_torch(q, k, v, rel_logits, dout, cu_seqlens_q, cu_seqlens_k, scale,
+                         rel_extent, causal=True, window_left=None, causal_align="reference",
+                         row_block=None):
+    """Gradients (dq, dk, dv, drel) of ``sum(rel_attn_torch(...) * dout)`` by torch autograd
+    (float32, CPU).  The reference has no backward; these are the gradients of its forward
+    (reference.py:4-39), which autograd differentiates exactly.  Rows without a visible key
+    (NaN in the reference's softmax) are given zero gradient, matching the kernels' zero
+    output for such rows."""
+    import torch
+
+    leaves = [t.detach().float().clone().requires_grad_(True) for t in (q, k, v, rel_logits)]
+    out = rel_attn_torch(*leaves, cu_seqlens_q, cu_seqlens_k, scale, rel_extent, causal=causal,
+                         window_left=window_left, causal_align=causal_align, row_block=row_block)
+    g = dout.detach().float().clone()
+    g[torch.isnan(out)] = 0.0
+    out = torch.nan_to_num(out, nan=0.0)
+    (out * g).sum().backward()
+    return tuple(torch.nan_to_num(t.grad, nan=0.0) for t in leaves)
