@@ -248,6 +248,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-window", action="store_true")
+    ap.add_argument("--no-backward", action="store_true")
     ap.add_argument("--extra-configs", action="store_true",
                     help="also time BASELINE configs 2 (ragged) and 4 (chunked)")
     ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
@@ -262,7 +263,7 @@ def main():
     if args.only == "prefill":
         args.no_decode = True
     if args.only == "decode":
-        args.no_e2e = args.no_window = True
+        args.no_e2e = args.no_window = args.no_backward = True
     if args.warmup < 3:
         args.warmup = 3
 
@@ -438,6 +439,38 @@ def main():
         result["window32k"] = {"value": world * wflops * args.steps / (wms / 1e3) / 1e12,
                                "unit": "TFLOP/s", "ms_per_step": wms / args.steps,
                                "window_left": 4096, "flops_per_step_per_gpu": wflops}
+
+    # ---------------- backward of the headline prefill (not in the reference)
+    if not args.no_backward:
+        from inkling_fa4 import inkling_fa4_rel_attention_backward
+
+        bout, blse = inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S,
+                                                      R, return_lse=True)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1000 + rank)
+        bdout = torch.randn(c.q.shape, generator=gen, device=dev).to(torch.bfloat16)
+        bws = torch.empty(HQ * S * 4, dtype=torch.uint8, device=dev)
+        bufs = (torch.empty_like(c.q), torch.empty_like(c.k), torch.empty_like(c.v),
+                torch.empty_like(c.rel))
+
+        def bwd_step():
+            return inkling_fa4_rel_attention_backward(
+                bdout, c.q, c.k, c.v, c.rel, bout, blse, c.cu_q, c.cu_k, S, S, R, dq=bufs[0],
+                dk=bufs[1], dv=bufs[2], drel=bufs[3], workspace=bws)
+
+        bsteps = max(5, args.steps // 5)
+        bms = timed(bwd_step, bsteps, args.warmup, stream, dist, barrier)
+        bflops = 2.5 * flops  # 5 matrix products of the forward's size (the usual convention)
+        result["backward32k"] = {
+            "value": world * bflops * bsteps / (bms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": bms / bsteps, "steps": bsteps,
+            "flops_per_step_per_gpu": bflops,
+            "flops_note": "algorithmic 2.5x forward (S, dP, dV, dK, dQ); the kernels execute "
+                          "3.5x (S and dP are recomputed by the dQ kernel to avoid atomics)",
+            "kernels": "rel_attn_bwd_prep_kernel, rel_attn_bwd_dkdv_kernel, "
+                       "rel_attn_bwd_dq_kernel (3 launches per step)",
+            "gpu_launches": 3 * bsteps}
+        del bout, blse, bdout, bws, bufs
     del c
     torch.cuda.empty_cache()
 

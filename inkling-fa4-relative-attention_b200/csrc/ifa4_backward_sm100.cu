@@ -127,9 +127,9 @@ constexpr uint32_t kSmemV = kTile;
 constexpr uint32_t kSmemQ = 2 * kTile;   // 2 stages
 constexpr uint32_t kSmemDO = 4 * kTile;  // 2 stages
 constexpr uint32_t kSmemBar = 6 * kTile;
-// per elementwise warp: the lse (log2 domain) and Delta of its 64 query columns
+// per elementwise warp, two buffers of -lse (log2 domain) and Delta of its 64 query columns
 constexpr uint32_t kSmemVec = kSmemBar + 256;
-constexpr uint32_t kSmemBytes = kSmemVec + 8 * 128 * 4;
+constexpr uint32_t kSmemBytes = kSmemVec + 8 * 256 * 4;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
 
@@ -309,12 +309,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 4) >> 2;        // columns [64 half, 64 half + 64)
     const int r = quarter * 32 + lane;       // key row within the block
-    float* wvec = vec + (warp - 4) * 128;    // this warp's [lse2 64 | Delta 64]
+    float* wvec = vec + (warp - 4) * 256;    // this warp's [2 buffers][-lse2 64 | Delta 64]
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t t_s = tbase + lane_off + kColS + half * 64;
     const uint32_t t_dp = tbase + lane_off + kColDP + half * 64;
     const int ms = a.align_bottom_right ? sk - sq : 0;
     const int bs = a.align_bottom_right ? sk - sq : sq - sk;
+    // Column statistics of step (head h, query tile q0) for this warp's 64 columns: lane holds
+    // entries lane and lane + 32 of -lse (log2 domain) and of Delta.
+    auto load_stats = [&](int h, int q0, float (&v)[4]) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int qq = q0 + half * 64 + ((lane + 32 * k) & 63);
+        v[k] = 0.f;
+        if (qq < sq) {
+          const long long tok = q_start + qq;
+          v[k] = k < 2 ? -a.lse[static_cast<long long>(h) * a.lse_sh + tok * a.lse_st] * kLog2e
+                       : a.delta[static_cast<long long>(h) * a.total_q + tok];
+        }
+      }
+    };
+    auto store_stats = [&](uint32_t buf, const float (&v)[4]) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) wvec[buf * 128 + lane + 32 * k] = v[k];
+    };
     uint32_t sc = 0, ec = 0;
     bool ok = true;
     for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
@@ -333,108 +351,125 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
-      for (int g = 0; g < group && ok; ++g) {
+      const int steps = group * blk.n_q;  // (head g, query tile i) with i fastest
+      {
+        float v[4];
+        load_stats(kvh * group, blk.i_lo * kBM, v);
+        __syncwarp();
+        store_stats(sc & 1, v);
+      }
+      for (int n = 0; n < steps; ++n, ++sc) {
+        const int g = n / blk.n_q;
         const int h = kvh * group + g;
-        const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
-        uint16_t* drel_h = a.drel + static_cast<long long>(h) * a.drel_sh;
-        for (int i = 0; i < blk.n_q; ++i, ++sc) {
-          const int q0 = (blk.i_lo + i) * kBM;
-          // per-column statistics of this warp's 64 query columns: lse (log2 domain) and
-          // Delta, loaded by the warp itself (read back as broadcasts)
-          __syncwarp();  // the previous step's reads are done
+        const int q0 = (blk.i_lo + n - g * blk.n_q) * kBM;
+        __syncwarp();  // this step's statistics are in wvec[sc & 1]
+        const float* nl = wvec + (sc & 1) * 128;  // -lse2 of the 64 columns
+        const float* dl = nl + 64;                // Delta
+        // visible columns of this key: q in [c_lo, c_hi) relative to q0
+        int c_lo = a.causal ? kl - ms - q0 : -0x40000000;
+        int c_hi = sq - q0;
+        if (a.window_left >= 0) c_hi = min(c_hi, kl - ms + a.window_left - q0 + 1);
+        if (!key_valid) c_hi = -0x40000000;
+        const bool has_mask = c_lo > half * 64 || c_hi < half * 64 + 64;
+        // bias distance of column c (absolute 0..127): dq0 + c
+        const int dq0 = q0 + bs - kl;
+        const bool has_bias = key_valid && dq0 + half * 64 <= a.rel_extent - 1 &&
+                              dq0 + half * 64 + 63 >= 0;
+        const bool warp_bias = __any_sync(0xffffffffu, has_bias);
+        const bool warp_slow = __any_sync(0xffffffffu, has_mask || has_bias);
+        if (!(ok = mbar_wait_warp(&bars->s_full, sc & 1, ab))) break;
+        tc_fence_after();
+        {
+          float p[64];
+          uint32_t sr[64];
+          tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(sr));
+          tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+          tmem_wait_ld();
+          if (!warp_slow) {  // interior tile: p = 2^(s * scale * log2e - lse2)
 #pragma unroll
-          for (int i = lane; i < 128; i += 32) {
-            const int qq = q0 + half * 64 + (i & 63);
-            float v = 0.f;
-            if (qq < sq) {
-              const long long tok = q_start + qq;
-              v = i < 64 ? a.lse[static_cast<long long>(h) * a.lse_sh + tok * a.lse_st] * kLog2e
-                         : a.delta[static_cast<long long>(h) * a.total_q + tok];
+            for (int c = 0; c < 64; c += 4) {
+              const float4 L = *reinterpret_cast<const float4*>(nl + c);
+              p[c] = fast_exp2(fmaf(__uint_as_float(sr[c]), a.scale_log2, L.x));
+              p[c + 1] = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), a.scale_log2, L.y));
+              p[c + 2] = fast_exp2(fmaf(__uint_as_float(sr[c + 2]), a.scale_log2, L.z));
+              p[c + 3] = fast_exp2(fmaf(__uint_as_float(sr[c + 3]), a.scale_log2, L.w));
             }
-            wvec[i] = v;
+          } else {
+            const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
+#pragma unroll
+            for (int c16 = 0; c16 < 64; c16 += 16) {  // 16 bias loads in flight at a time
+#pragma unroll
+              for (int c = c16; c < c16 + 16; ++c) {
+                const int cq = half * 64 + c;
+                float bias = 0.f;
+                if (warp_bias) {
+                  const int d = dq0 + cq;
+                  if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
+                    bias = bf16_bits_to_float(
+                        __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
+                }
+                p[c] = fast_exp2(fmaf(__uint_as_float(sr[c]), a.scale_log2, fmaf(bias, kLog2e, nl[c])));
+                if (has_mask && (cq < c_lo || cq >= c_hi)) p[c] = 0.f;
+              }
+              __syncwarp();
+            }
+          }
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
+          __syncwarp();
+          tmem_st32(t_s, pk);  // P^T over this half's first 32 columns (all 64 already read)
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full);
+        // the next step's statistics, in flight while dS is computed
+        const bool has_next = n + 1 < steps;
+        float nv[4];
+        if (has_next) {
+          const int g1 = (n + 1) / blk.n_q;
+          load_stats(kvh * group + g1, (blk.i_lo + n + 1 - g1 * blk.n_q) * kBM, nv);
+        }
+        if (!(ok = mbar_wait_warp(&bars->dp_full, sc & 1, ab))) break;
+        tc_fence_after();
+        // dS^T = P^T (dP^T - Delta) from the bf16 P^T in TMEM (the dV operand; the next S^T
+        // overwrites it only after dK is issued), 32 columns at a time, in place over dP^T
+        uint16_t* drel_h = a.drel + static_cast<long long>(h) * a.drel_sh;
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t dr[32], pr[16];
+          tmem_ld32(t_dp + c2 * 32, dr);
+          tmem_ld16(t_s + c2 * 16, pr);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float4 D = *reinterpret_cast<const float4*>(dl + c2 * 32 + 2 * i);
+            pk[i] = pack_bf16x2(__uint_as_float(pr[i] << 16) * (__uint_as_float(dr[2 * i]) - D.x),
+                                __uint_as_float(pr[i] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 1]) - D.y));
+            pk[i + 1] = pack_bf16x2(
+                __uint_as_float(pr[i + 1] << 16) * (__uint_as_float(dr[2 * i + 2]) - D.z),
+                __uint_as_float(pr[i + 1] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 3]) - D.w));
           }
           __syncwarp();
-          const float* lse2 = wvec;
-          const float* dlt = wvec + 64;
-          // visible columns of this key: q in [c_lo, c_hi) relative to q0
-          int c_lo = a.causal ? kl - ms - q0 : -0x40000000;
-          int c_hi = sq - q0;
-          if (a.window_left >= 0) c_hi = min(c_hi, kl - ms + a.window_left - q0 + 1);
-          if (!key_valid) c_hi = -0x40000000;
-          const bool has_mask = c_lo > half * 64 || c_hi < half * 64 + 64;
-          // bias distance of column c (absolute 0..127): dq0 + c
-          const int dq0 = q0 + bs - kl;
-          const bool has_bias = key_valid && dq0 + half * 64 <= a.rel_extent - 1 &&
-                                dq0 + half * 64 + 63 >= 0;
-          if (!(ok = mbar_wait_warp(&bars->s_full, sc & 1, ab))) break;
-          tc_fence_after();
-          // P^T, 32 columns at a time; chunk c2's bf16 pairs go to columns [16 c2, 16 c2 + 16)
-          // of this half, which the chunks read so far already cover
-          float p[64];
-          const bool warp_bias = __any_sync(0xffffffffu, has_bias);
-#pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2) {
-            uint32_t sr[32];
-            tmem_ld32(t_s + c2 * 32, sr);
-            tmem_wait_ld();
+          tmem_st16(t_dp + c2 * 16, pk);  // columns [16 c2, 16 c2 + 16): already read
+          if (warp_bias) {  // d rel: this key's band entries (dS of masked pairs is 0)
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const int c = c2 * 32 + i;
-              const int cq = half * 64 + c;
-              float bias = 0.f;
-              if (warp_bias) {
-                const int d = dq0 + cq;
-                if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
-                  bias = bf16_bits_to_float(
-                      __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
-              }
-              p[c] = fast_exp2(fmaf(__uint_as_float(sr[i]), a.scale_log2, bias * kLog2e - lse2[c]));
-              if (has_mask && (cq < c_lo || cq >= c_hi)) p[c] = 0.f;
-            }
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(p[c2 * 32 + 2 * i], p[c2 * 32 + 2 * i + 1]);
-            __syncwarp();
-            tmem_st16(t_s + c2 * 16, pk);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->p_full);
-          if (!(ok = mbar_wait_warp(&bars->dp_full, sc & 1, ab))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2) {  // dS^T, in place over dP^T as for P^T
-            uint32_t dr[32];
-            tmem_ld32(t_dp + c2 * 32, dr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              p[c2 * 32 + i] *= __uint_as_float(dr[i]) - dlt[c2 * 32 + i];
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(p[c2 * 32 + 2 * i], p[c2 * 32 + 2 * i + 1]);
-            __syncwarp();
-            tmem_st16(t_dp + c2 * 16, pk);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->ds_full);
-          // d rel: the band entries of this key (dS of masked pairs is 0)
-          if (warp_bias) {
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-              const int cq = half * 64 + c;
+              const int cq = half * 64 + c2 * 32 + i;
               const int d = dq0 + cq;
-              if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0) {
-                __nv_bfloat16 v = __float2bfloat16_rn(p[c]);
+              if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
                 drel_h[static_cast<long long>(q_start + q0 + cq) * a.drel_st + d] =
-                    *reinterpret_cast<uint16_t*>(&v);
-              }
+                    static_cast<uint16_t>((i & 1) ? (pk[i >> 1] >> 16) : (pk[i >> 1] & 0xffffu));
             }
           }
         }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_full);
+        if (has_next) store_stats((sc + 1) & 1, nv);  // that buffer's last reader was step n - 1
       }
       if (!ok) break;
       // epilogue: dV and scale * dK of this thread's key row, half of the columns
