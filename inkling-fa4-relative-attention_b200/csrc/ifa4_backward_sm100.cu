@@ -29,9 +29,9 @@
 //                              from TMEM.
 // dK / dV / dQ are written once per CTA (no atomics), so the backward is deterministic.
 //
-// Warp roles in both tensor-core kernels (384 threads): warp 0 TMA producer, warp 1 UMMA issuer
-// (one thread), warp 2 TMEM owner, warps 4-11 elementwise: warp w handles TMEM lanes
-// 32 (w % 4) .. +31 (one row each) and columns 64 ((w - 4) / 4) .. +63 of the 128-column tile.
+// Warp roles in both tensor-core kernels (320 threads): warp 0 TMA producer, warp 1 UMMA issuer (one thread) and TMEM owner,
+// warps 2-9 elementwise: warp w handles TMEM lanes 32 (w % 4) .. +31 (one row each) and columns
+// 64 ((w - 2) / 4) .. +63 of the 128-column tile.
 // There is no row reduction in the backward, so splitting columns between warps is free.
 // All waits are bounded (status word on timeout), as in the forward kernels.
 #include <cuda.h>
@@ -47,13 +47,19 @@ namespace bwd {
 
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // keys per tile
-constexpr int kThreads = 384;
+constexpr int kThreads = 320;
 constexpr uint32_t kHalf = 128u * 128u;  // 128 rows x 128 B (64 dims)
 constexpr uint32_t kTile = 2u * kHalf;   // 128 rows x 256 B (128 dims)
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kIdescKM = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescMN = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
+// Of every 16 probabilities the dK/dV kernel's interior path computes, this many use the
+// FMA-pipe exp2 polynomial (exp2_poly_pair) instead of the SFU: the P phase is SFU-bound
+// (exp2 plus the bf16 packing), so moving part of it to the FMA pipe shortens it.
+constexpr int kBwdEmuOf16 = 0;
+#define PACK_P pack_bf16x2
+#define PACK_DS pack_bf16x2
 
 // D[128 x 128] = A B^T over 128 dims, A and B K-major 128-row tiles (two swizzled halves).
 __device__ __forceinline__ void mma_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
@@ -76,6 +82,16 @@ __device__ __forceinline__ void mma_tk(uint32_t d_tmem, uint32_t a_tmem, uint32_
   for (int kk = 0; kk < 8; ++kk)
     umma_ts(d_tmem, a_tmem + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_advance(bd, kk * 2048),
             kIdescMN, (kk > 0 || accumulate) ? 1u : 0u);
+}
+
+// Two non-negative finite floats -> packed bf16x2 (lo in the low half), rounded to nearest even
+// with integer ALU operations (add 0x7fff plus the kept LSB, keep the high halves), which keeps
+// the conversions off the SFU-shared conversion path in the SFU-bound elementwise phases.
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+  const uint32_t ra = a + 0x7fffu + ((a >> 16) & 1u);
+  const uint32_t rb = b + 0x7fffu + ((b >> 16) & 1u);
+  return __byte_perm(ra, rb, 0x7632);
 }
 
 __device__ __forceinline__ void store_row64_bf16(uint16_t* dst, const float* v, float mul) {
@@ -205,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 2) {
+  if (warp == 1) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -279,7 +295,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (blk.n_q == 0) continue;
         if (!(ok = mbar_wait(&bars->kv_full, ic & 1, ab))) break;
         const int steps = group * blk.n_q;
-        for (int n = 0; n < steps; ++n, ++sc) {
+        // Issue order per step n: dV(n) once P^T(n) is in TMEM; then, once dS^T(n) is, the
+        // next step's S^T(n+1) (its region's last readers, the dS phase and dV(n), are done or
+        // queued before it) ahead of dK(n) and dP^T(n+1), so the elementwise warps' P phase of
+        // step n+1 runs while the tensor core computes dK(n) and dP^T(n+1).
+        {
           const uint32_t st = sc & 1;
           if (!(ok = mbar_wait(&bars->qdo_full[st], (sc >> 1) & 1, ab))) break;
           tc_fence_after();
@@ -287,14 +307,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&bars->s_full);
           mma_kk(tbase + kColDP, v_addr, do_addr + st * kTile);  // dP^T = V dO^T
           umma_commit(&bars->dp_full);
+        }
+        for (int n = 0; n < steps; ++n, ++sc) {
+          const uint32_t st = sc & 1;
           if (n == 0 && !(ok = mbar_wait(&bars->acc_empty, (ic & 1) ^ 1, ab))) break;
           if (!(ok = mbar_wait(&bars->p_full, sc & 1, ab))) break;
           tc_fence_after();
           mma_tk(tbase + kColDV, tbase + kColS, do_addr + st * kTile, n > 0);  // dV += P^T dO
           if (!(ok = mbar_wait(&bars->ds_full, sc & 1, ab))) break;
+          const bool next = n + 1 < steps;
+          const uint32_t sn = (sc + 1) & 1;
+          if (next && !(ok = mbar_wait(&bars->qdo_full[sn], ((sc + 1) >> 1) & 1, ab))) break;
           tc_fence_after();
+          if (next) {
+            mma_kk(tbase + kColS, k_addr, q_addr + sn * kTile);  // S^T(n+1)
+            umma_commit(&bars->s_full);
+          }
           mma_tk(tbase + kColDK, tbase + kColDP, q_addr + st * kTile, n > 0);  // dK += dS^T Q
           umma_commit(&bars->qdo_empty[st]);
+          if (next) {
+            mma_kk(tbase + kColDP, v_addr, do_addr + sn * kTile);  // dP^T(n+1)
+            umma_commit(&bars->dp_full);
+          }
         }
         if (!ok) break;
         umma_commit(&bars->acc_full);
@@ -304,12 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, ab);
     }
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------------ elementwise + epilogue
     const int quarter = warp & 3;
-    const int half = (warp - 4) >> 2;        // columns [64 half, 64 half + 64)
+    const int half = (warp - 2) >> 2;        // columns [64 half, 64 half + 64)
     const int r = quarter * 32 + lane;       // key row within the block
-    float* wvec = vec + (warp - 4) * 256;    // this warp's [2 buffers][-lse2 64 | Delta 64]
+    float* wvec = vec + (warp - 2) * 256;    // this warp's [2 buffers][-lse2 64 | Delta 64]
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t t_s = tbase + lane_off + kColS + half * 64;
     const uint32_t t_dp = tbase + lane_off + kColDP + half * 64;
@@ -377,6 +411,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                               dq0 + half * 64 + 63 >= 0;
         const bool warp_bias = __any_sync(0xffffffffu, has_bias);
         const bool warp_slow = __any_sync(0xffffffffu, has_mask || has_bias);
+        // -lse2 of the 64 columns into registers while S^T is computed: during the P phase the
+        // tensor core streams dK / dP^T operands out of shared memory, and column loads issued
+        // then stall the exponentials behind them
+        float nlr[64];
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+          const float4 L = *reinterpret_cast<const float4*>(nl + c);
+          nlr[c] = L.x;
+          nlr[c + 1] = L.y;
+          nlr[c + 2] = L.z;
+          nlr[c + 3] = L.w;
+        }
         if (!(ok = mbar_wait_warp(&bars->s_full, sc & 1, ab))) break;
         tc_fence_after();
         {
@@ -387,12 +433,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
           if (!warp_slow) {  // interior tile: p = 2^(s * scale * log2e - lse2)
 #pragma unroll
-            for (int c = 0; c < 64; c += 4) {
-              const float4 L = *reinterpret_cast<const float4*>(nl + c);
-              p[c] = fast_exp2(fmaf(__uint_as_float(sr[c]), a.scale_log2, L.x));
-              p[c + 1] = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), a.scale_log2, L.y));
-              p[c + 2] = fast_exp2(fmaf(__uint_as_float(sr[c + 2]), a.scale_log2, L.z));
-              p[c + 3] = fast_exp2(fmaf(__uint_as_float(sr[c + 3]), a.scale_log2, L.w));
+            for (int c = 0; c < 64; c += 2) {
+              const float x0 = fmaf(__uint_as_float(sr[c]), a.scale_log2, nlr[c]);
+              const float x1 = fmaf(__uint_as_float(sr[c + 1]), a.scale_log2, nlr[c + 1]);
+              if ((c & 15) < kBwdEmuOf16) exp2_poly_pair(x0, x1, p[c], p[c + 1]);
+              else {
+                p[c] = fast_exp2(x0);
+                p[c + 1] = fast_exp2(x1);
+              }
             }
           } else {
             const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
@@ -408,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bias = bf16_bits_to_float(
                         __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
                 }
-                p[c] = fast_exp2(fmaf(__uint_as_float(sr[c]), a.scale_log2, fmaf(bias, kLog2e, nl[c])));
+                p[c] = fast_exp2(fmaf(__uint_as_float(sr[c]), a.scale_log2, fmaf(bias, kLog2e, nlr[c])));
                 if (has_mask && (cq < c_lo || cq >= c_hi)) p[c] = 0.f;
               }
               __syncwarp();
@@ -416,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint32_t pk[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
+          for (int i = 0; i < 32; ++i) pk[i] = PACK_P(p[2 * i], p[2 * i + 1]);
           __syncwarp();
           tmem_st32(t_s, pk);  // P^T over this half's first 32 columns (all 64 already read)
         }
@@ -431,6 +479,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int g1 = (n + 1) / blk.n_q;
           load_stats(kvh * group + g1, (blk.i_lo + n + 1 - g1 * blk.n_q) * kBM, nv);
         }
+        float dlr[64];  // Delta of the 64 columns, loaded before the wait as -lse2 above
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+          const float4 D = *reinterpret_cast<const float4*>(dl + c);
+          dlr[c] = D.x;
+          dlr[c + 1] = D.y;
+          dlr[c + 2] = D.z;
+          dlr[c + 3] = D.w;
+        }
         if (!(ok = mbar_wait_warp(&bars->dp_full, sc & 1, ab))) break;
         tc_fence_after();
         // dS^T = P^T (dP^T - Delta) from the bf16 P^T in TMEM (the dV operand; the next S^T
@@ -444,13 +501,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            const float4 D = *reinterpret_cast<const float4*>(dl + c2 * 32 + 2 * i);
-            pk[i] = pack_bf16x2(__uint_as_float(pr[i] << 16) * (__uint_as_float(dr[2 * i]) - D.x),
-                                __uint_as_float(pr[i] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 1]) - D.y));
-            pk[i + 1] = pack_bf16x2(
-                __uint_as_float(pr[i + 1] << 16) * (__uint_as_float(dr[2 * i + 2]) - D.z),
-                __uint_as_float(pr[i + 1] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 3]) - D.w));
+          for (int i = 0; i < 16; ++i) {
+            const float* D = dlr + c2 * 32 + 2 * i;
+            pk[i] = PACK_DS(__uint_as_float(pr[i] << 16) * (__uint_as_float(dr[2 * i]) - D[0]),
+                            __uint_as_float(pr[i] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 1]) - D[1]));
           }
           __syncwarp();
           tmem_st16(t_dp + c2 * 16, pk);  // columns [16 c2, 16 c2 + 16): already read
@@ -506,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }
@@ -604,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 2) {
+  if (warp == 1) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -726,15 +780,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, ab);
     }
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------------ elementwise + epilogue
     const int quarter = warp & 3;
-    const int half = (warp - 4) >> 2;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int ms = a.align_bottom_right ? sk - sq : 0;
     const int bs = a.align_bottom_right ? sk - sq : sq - sk;
-    uint16_t* bias_buf = reinterpret_cast<uint16_t*>(smem + kSmemBias + (warp - 4) * kBiasWarpBytes);
+    uint16_t* bias_buf = reinterpret_cast<uint16_t*>(smem + kSmemBias + (warp - 2) * kBiasWarpBytes);
     uint32_t sc = 0, ec = 0;
     bool ok = true;
     for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
@@ -862,7 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }
