@@ -54,12 +54,6 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kIdescKM = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescMN = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
-// Of every 16 probabilities the dK/dV kernel's interior path computes, this many use the
-// FMA-pipe exp2 polynomial (exp2_poly_pair) instead of the SFU: the P phase is SFU-bound
-// (exp2 plus the bf16 packing), so moving part of it to the FMA pipe shortens it.
-constexpr int kBwdEmuOf16 = 0;
-#define PACK_P pack_bf16x2
-#define PACK_DS pack_bf16x2
 
 // D[128 x 128] = A B^T over 128 dims, A and B K-major 128-row tiles (two swizzled halves).
 __device__ __forceinline__ void mma_kk(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
@@ -82,16 +76,6 @@ __device__ __forceinline__ void mma_tk(uint32_t d_tmem, uint32_t a_tmem, uint32_
   for (int kk = 0; kk < 8; ++kk)
     umma_ts(d_tmem, a_tmem + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_advance(bd, kk * 2048),
             kIdescMN, (kk > 0 || accumulate) ? 1u : 0u);
-}
-
-// Two non-negative finite floats -> packed bf16x2 (lo in the low half), rounded to nearest even
-// with integer ALU operations (add 0x7fff plus the kept LSB, keep the high halves), which keeps
-// the conversions off the SFU-shared conversion path in the SFU-bound elementwise phases.
-__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  const uint32_t ra = a + 0x7fffu + ((a >> 16) & 1u);
-  const uint32_t rb = b + 0x7fffu + ((b >> 16) & 1u);
-  return __byte_perm(ra, rb, 0x7632);
 }
 
 __device__ __forceinline__ void store_row64_bf16(uint16_t* dst, const float* v, float mul) {
@@ -426,45 +410,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait_warp(&bars->s_full, sc & 1, ab))) break;
         tc_fence_after();
         {
-          float p[64];
-          uint32_t sr[64];
-          tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(sr));
-          tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-          tmem_wait_ld();
-          if (!warp_slow) {  // interior tile: p = 2^(s * scale * log2e - lse2)
-#pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-              const float x0 = fmaf(__uint_as_float(sr[c]), a.scale_log2, nlr[c]);
-              const float x1 = fmaf(__uint_as_float(sr[c + 1]), a.scale_log2, nlr[c + 1]);
-              if ((c & 15) < kBwdEmuOf16) exp2_poly_pair(x0, x1, p[c], p[c + 1]);
-              else {
-                p[c] = fast_exp2(x0);
-                p[c + 1] = fast_exp2(x1);
-              }
-            }
-          } else {
-            const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
-#pragma unroll
-            for (int c16 = 0; c16 < 64; c16 += 16) {  // 16 bias loads in flight at a time
-#pragma unroll
-              for (int c = c16; c < c16 + 16; ++c) {
-                const int cq = half * 64 + c;
-                float bias = 0.f;
-                if (warp_bias) {
-                  const int d = dq0 + cq;
-                  if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
-                    bias = bf16_bits_to_float(
-                        __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
-                }
-                p[c] = fast_exp2(fmaf(__uint_as_float(sr[c]), a.scale_log2, fmaf(bias, kLog2e, nlr[c])));
-                if (has_mask && (cq < c_lo || cq >= c_hi)) p[c] = 0.f;
-              }
-              __syncwarp();
-            }
-          }
+          // P^T, 32 columns at a time, packed to bf16 pairs as they are produced
           uint32_t pk[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) pk[i] = PACK_P(p[2 * i], p[2 * i + 1]);
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t sr[32];
+            tmem_ld32(t_s + c2 * 32, sr);
+            tmem_wait_ld();
+            if (!warp_slow) {  // interior tile: p = 2^(s * scale * log2e - lse2)
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float x0 = fmaf(__uint_as_float(sr[i]), a.scale_log2, nlr[c2 * 32 + i]);
+                const float x1 = fmaf(__uint_as_float(sr[i + 1]), a.scale_log2, nlr[c2 * 32 + i + 1]);
+                pk[c2 * 16 + i / 2] = pack_bf16x2(fast_exp2(x0), fast_exp2(x1));
+              }
+            } else {
+              const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
+#pragma unroll
+              for (int i16 = 0; i16 < 32; i16 += 16) {  // 16 bias loads in flight at a time
+                float p[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int c = c2 * 32 + i16 + i;
+                  const int cq = half * 64 + c;
+                  float bias = 0.f;
+                  if (warp_bias) {
+                    const int d = dq0 + cq;
+                    if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
+                      bias = bf16_bits_to_float(
+                          __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
+                  }
+                  p[i] = fast_exp2(fmaf(__uint_as_float(sr[i16 + i]), a.scale_log2,
+                                        fmaf(bias, kLog2e, nlr[c])));
+                  if (has_mask && (cq < c_lo || cq >= c_hi)) p[i] = 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) pk[c2 * 16 + i16 / 2 + i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
+                __syncwarp();
+              }
+            }
+          }
           __syncwarp();
           tmem_st32(t_s, pk);  // P^T over this half's first 32 columns (all 64 already read)
         }
@@ -503,8 +488,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float* D = dlr + c2 * 32 + 2 * i;
-            pk[i] = PACK_DS(__uint_as_float(pr[i] << 16) * (__uint_as_float(dr[2 * i]) - D[0]),
-                            __uint_as_float(pr[i] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 1]) - D[1]));
+            pk[i] = pack_bf16x2(__uint_as_float(pr[i] << 16) * (__uint_as_float(dr[2 * i]) - D[0]),
+                                __uint_as_float(pr[i] & 0xffff0000u) * (__uint_as_float(dr[2 * i + 1]) - D[1]));
           }
           __syncwarp();
           tmem_st16(t_dp + c2 * 16, pk);  // columns [16 c2, 16 c2 + 16): already read
