@@ -238,9 +238,19 @@ int ifa4_backward_workspace_size(const IFA4BackwardParams* params, size_t* bytes
 int ifa4_backward_launch(const IFA4BackwardParams* params, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Self-test of the failure detection (test hook; the reference has no counterpart): launches
+ * on `stream` a kernel whose barrier wait can never complete, so the kernels' bounded-wait path
+ * runs out after timeout_ns (0 < timeout_ns <= 1e9).  Afterwards the status word holds exactly
+ * bit 3 (value 8): one waiter timed out and the other left through the abort flag it raised
+ * (bit 4 would mean the abort did not propagate).  Nothing faults; the context stays usable.
+ * Run it alone: while the status word is nonzero, concurrently running kernels of this library
+ * abandon their waits too (that is how one failure stops the others). */
+int ifa4_selftest_bounded_wait(int64_t timeout_ns, void* stream);
+
 /* Reads (and optionally clears) the library's device status word on `stream`, blocking the
  * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on
- * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode, bit 2 backward.  Test hook; the
+ * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode, bit 2 backward, bits 3-4
+ * ifa4_selftest_bounded_wait.  Test hook; the
  * reference has no counterpart. */
 int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out);
 

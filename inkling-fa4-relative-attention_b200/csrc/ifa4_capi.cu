@@ -11,6 +11,7 @@
 
 #include "../../include/inkling_fa4.h"
 #include "ifa4_internal.h"
+#include "ifa4_ptx.cuh"
 
 namespace {
 
@@ -30,6 +31,34 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 // Device status word: kernels OR IFA4 status bits into it when they abandon a bounded wait.
 __device__ int g_ifa4_device_status;
+
+// Exercises the bounded-wait path of the kernels on a barrier that nothing ever arrives on:
+// warp 0 (one thread) gives up after timeout_ns and raises kStatusSelfTestTimeout; warp 1
+// (warp-collective wait) has ten times the limit and must leave through the abort flag that
+// warp 0 raised, never through its own timeout (kStatusSelfTestOwnTimeout).
+__global__ void __launch_bounds__(64) ifa4_selftest_wait_kernel(int* status,
+                                                                unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    ifa4::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ifa4::fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if ((threadIdx.x & 31) == 0) {
+      const ifa4::AbortCtx ab{&abort_flag, status, ifa4::kStatusSelfTestTimeout};
+      ifa4::mbar_wait(&bar, 0, ab, timeout_ns);
+    }
+  } else {
+    const ifa4::AbortCtx ab{&abort_flag, status, ifa4::kStatusSelfTestOwnTimeout};
+    ifa4::mbar_wait_warp(&bar, 0, ab, 10 * timeout_ns);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ifa4::mbar_arrive(&bar);  // complete the phase before the CTA exits
+}
 
 constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {nullptr};
@@ -646,6 +675,20 @@ int ifa4_backward_launch(const IFA4BackwardParams* p, void* workspace, size_t wo
                                               static_cast<int>(ks),
                                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+  return IFA4_OK;
+}
+
+int ifa4_selftest_bounded_wait(int64_t timeout_ns, void* stream) {
+  g_last_error[0] = '\0';
+  if (timeout_ns <= 0 || timeout_ns > 1000000000LL)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "selftest: timeout_ns must be in (0, 1e9]");
+  int* status = nullptr;
+  int rc = device_status_ptr(&status);
+  if (rc) return rc;
+  ifa4_selftest_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<unsigned long long>(timeout_ns));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
   return IFA4_OK;
 }
 

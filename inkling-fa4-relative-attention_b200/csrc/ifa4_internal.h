@@ -13,6 +13,8 @@ constexpr int kHeadDim = 128;
 constexpr int kStatusPrefillTimeout = 1;
 constexpr int kStatusDecodeTimeout = 2;
 constexpr int kStatusBackwardTimeout = 4;
+constexpr int kStatusSelfTestTimeout = 8;   // ifa4_selftest_bounded_wait, warp 0
+constexpr int kStatusSelfTestOwnTimeout = 16;  // ifa4_selftest_bounded_wait, warp 1 (must not be set)
 
 struct PrefillKernelArgs {
   const uint16_t* rel;       // bf16 bits

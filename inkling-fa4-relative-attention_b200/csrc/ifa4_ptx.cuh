@@ -93,7 +93,8 @@ __device__ __forceinline__ void raise_abort(const AbortCtx& a) {
 }
 
 // Single-thread bounded wait.  Returns false if the wait was abandoned (timeout or abort).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const AbortCtx& a) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const AbortCtx& a,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
@@ -101,7 +102,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     if (mbar_try_wait(addr, parity)) return true;
     if ((it & 255u) == 0) {
       if (abort_requested(a)) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
         raise_abort(a);
         return false;
       }
@@ -110,7 +111,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
 }
 
 // Warp-collective bounded wait: every lane polls, the outcome is warp-uniform.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const AbortCtx& a) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const AbortCtx& a,
+                                               unsigned long long timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (__all_sync(0xffffffffu, mbar_try_wait(addr, parity))) return true;
   const unsigned long long t0 = globaltimer_ns();
@@ -121,7 +123,7 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, c
       if (lane_id() == 0) {
         if (abort_requested(a)) {
           give_up = 1;
-        } else if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        } else if (globaltimer_ns() - t0 > timeout_ns) {
           raise_abort(a);
           give_up = 1;
         }

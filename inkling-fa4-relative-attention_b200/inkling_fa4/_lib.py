@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "ifa4_backward_launch",
     "ifa4_backward_workspace_size",
     "ifa4_read_device_status",
+    "ifa4_selftest_bounded_wait",
     "ifa4_prefill_tile_config_name",
     "ifa4_last_error_string",
     "ifa4_abi_version",
@@ -128,6 +129,8 @@ def lib() -> ctypes.CDLL:
     L.ifa4_backward_launch.restype = ctypes.c_int
     L.ifa4_backward_workspace_size.argtypes = [ctypes.POINTER(BackwardParams), ctypes.POINTER(sz)]
     L.ifa4_backward_workspace_size.restype = ctypes.c_int
+    L.ifa4_selftest_bounded_wait.argtypes = [ctypes.c_int64, vp]
+    L.ifa4_selftest_bounded_wait.restype = ctypes.c_int
     L.ifa4_read_device_status.argtypes = [vp, i32, ctypes.POINTER(i32)]
     L.ifa4_read_device_status.restype = ctypes.c_int
     L.ifa4_prefill_tile_config_name.argtypes = [i32]

@@ -190,3 +190,9 @@ def test_page_kv_roundtrip():
             mask[int(bt[b, j // 16]), j % 16] = True
     assert bool(torch.isnan(pc.k[~mask].float()).all()) and bool(torch.isnan(pc.v[~mask].float()).all())
     assert np.isfinite(pc.k[mask].float().numpy()).all()
+
+
+def test_selftest_limit_validated_before_any_cuda_call():
+    L = _lib.lib()
+    assert L.ifa4_selftest_bounded_wait(0, None) == _lib.IFA4_ERR_INVALID_ARGUMENT
+    assert b"timeout_ns" in L.ifa4_last_error_string()
