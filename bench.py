@@ -84,15 +84,20 @@ class ClockSampler:
     def __init__(self, uuids):
         self.uuids = [u.lower() for u in uuids]
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f".clocks_{os.getpid()}.csv")
+        self.lines = []
+
+    def _drain(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def start(self):
+        import threading
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._drain, daemon=True)
+            self.reader.start()
         except Exception:
             self.proc = None
 
@@ -104,9 +109,9 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        self.fh.close()
+        self.reader.join(timeout=5)
         rows = []
-        for line in open(self.path):
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
                 continue
@@ -114,10 +119,6 @@ class ClockSampler:
             if self.uuids and not any(u in uuid or uuid in u for u in self.uuids):
                 continue
             rows.append(parts)
-        try:
-            os.remove(self.path)
-        except OSError:
-            pass
         if not rows:
             return None
         sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]

@@ -1,9 +1,8 @@
 """Generate golden fixtures by running the reference's own oracle ``ref_rel_attn``.
 
-Run in a container that has the reference checkout (default ``/root/reference``; override
-with ``--reference``):
+Run in a container that has the reference checkout:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 It imports ``src/inkling_fa4/reference.py`` by file path (that file needs only torch), builds
 seeded inputs with ``inkling_fa4.workloads.make_case``, and stores, per case, the metadata
@@ -99,7 +98,7 @@ def load_reference(path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="reference checkout (its src/inkling_fa4/reference.py is imported)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     ref = load_reference(os.path.join(args.reference, "src", "inkling_fa4", "reference.py"))

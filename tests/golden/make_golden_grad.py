@@ -4,7 +4,7 @@ The reference has no backward pass; the gradients of its forward (src/inkling_fa
 :4-39, plain torch, so autograd differentiates it exactly) are what a backward kernel must
 reproduce.  Run in a container that has the reference checkout:
 
-    python tests/golden/make_golden_grad.py [--reference /root/reference]
+    python tests/golden/make_golden_grad.py --reference <reference checkout>
 
 Inputs are the seeded bf16 values of ``inkling_fa4.workloads.make_case`` taken to float32 (so a
 bf16 kernel sees the same numbers), ``dout`` is seeded N(0, 1) rounded to bf16, the loss is
@@ -65,7 +65,7 @@ def checksums(c, dout):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="reference checkout (its src/inkling_fa4/reference.py is imported)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     ref = load_reference(os.path.join(args.reference, "src", "inkling_fa4", "reference.py"))
