@@ -317,6 +317,8 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   const int group = p->n_heads / p->kv_heads;
   a.pair_heads = (group % 2 == 0) ? 1 : 0;
   a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  a.bias_vec = aligned16(p->rel) && p->rel_stride_t % 8 == 0 && p->rel_stride_h % 8 == 0 &&
+               p->rel_extent % 8 == 0;
   a.lse = p->lse;
   a.lse_sh = p->lse_stride_h;
   a.lse_st = p->lse_stride_t;

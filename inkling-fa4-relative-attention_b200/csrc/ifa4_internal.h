@@ -25,6 +25,8 @@ struct PrefillKernelArgs {
   long long out_st, out_sh;
   int batch, n_heads, kv_heads, rel_extent;
   int causal, window_left, align_bottom_right;
+  int bias_vec;              // rel 16-byte aligned (base, strides) and rel_extent % 8 == 0:
+                             // each row loads its bias with 16-byte vectors
   int pair_heads;            // 1: the CTA's two sub-tiles are two heads at the same rows
                              // 0: the CTA's two sub-tiles are consecutive 128-row blocks
   float scale_log2;          // softmax_scale * log2(e)
