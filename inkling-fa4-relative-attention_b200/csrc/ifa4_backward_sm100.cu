@@ -809,6 +809,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bl = dmax - a.rel_extent + 1 - k0;    // first column with bias
         const int bh = dmax - k0;                       // last column with bias
         const bool has_bias = row_valid && bl <= cb + 63 && bh >= cb;
+        // vector bias path: this row's windows for both chunks, loaded while S is computed
+        uint32_t bwin[2][20];
+        if (a.bias_vec && __any_sync(0xffffffffu, has_bias)) {
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            const int c0 = cb + c2 * 32;
+            load_bias_window(rel_row, bh, c0 >> 5, a.rel_extent,
+                             has_bias && c0 + 31 >= bl && c0 <= bh, bwin[c2]);
+          }
+        }
         if (!(ok = mbar_wait_warp(&bars->s_full[sc & 1], (sc >> 1) & 1, ab))) break;
         tc_fence_after();
         float p[64];
@@ -822,7 +832,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(sr[i]) * a.scale_log2 - lse2;
           const int c0 = cb + c2 * 32;  // absolute first column of this chunk
           const bool chunk_bias = has_bias && c0 + 31 >= bl && c0 <= bh;
-          if (__any_sync(0xffffffffu, chunk_bias)) {
+          if (a.bias_vec) {
+            if (__any_sync(0xffffffffu, chunk_bias)) add_bias_window(bwin[c2], bh, c0 >> 5, x);
+          } else if (__any_sync(0xffffffffu, chunk_bias)) {
             // the warp gathers its 32 rows' bias for these 32 columns (coalesced row reads),
             // transposes through shared memory, and each lane adds its own row
             uint16_t v[32];

@@ -650,6 +650,8 @@ int ifa4_backward_launch(const IFA4BackwardParams* p, void* workspace, size_t wo
   a.align_bottom_right = p->causal_align == IFA4_ALIGN_BOTTOM_RIGHT;
   a.scale = p->softmax_scale;
   a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  a.bias_vec = aligned16(p->rel) && p->rel_stride_t % 8 == 0 && p->rel_stride_h % 8 == 0 &&
+               p->rel_extent % 8 == 0;
   a.status = status;
 
   CUtensorMap tq, tk, tv, tdo;

@@ -113,6 +113,7 @@ struct BackwardKernelArgs {
   int causal, window_left, align_bottom_right;
   float scale;               // softmax_scale
   float scale_log2;          // softmax_scale * log2(e)
+  int bias_vec;              // rel 16-byte aligned and rel_extent % 8 == 0 (vector bias windows)
   int* status;
 };
 

@@ -238,47 +238,6 @@ __device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_
   }
 }
 
-// Vector bias path (rel 16-byte aligned, rel_extent a multiple of 8): chunk cc (columns
-// [32 cc, 32 cc + 32)) of a tile whose column 0 sits at bias distance dtop needs this row's
-// distances [dtop - 32 cc - 31, dtop - 32 cc].  The 40-element window from the 8-aligned
-// distance below that range is loaded as five 16-byte vectors; a vector is either wholly inside
-// [0, rel_extent) or wholly outside it (then zero, not read), so nothing outside the row's
-// rel_extent elements is touched.
-__device__ __forceinline__ void load_bias_window(const uint16_t* rel_row, int dtop, int cc,
-                                                 int rel_extent, bool active, uint32_t (&w)[20]) {
-  const int base = (dtop - 32 * cc - 31) & ~7;
-#pragma unroll
-  for (int v = 0; v < 5; ++v) {
-    const int st = base + 8 * v;
-    uint4 x = make_uint4(0u, 0u, 0u, 0u);
-    if (active && st >= 0 && st < rel_extent) x = ldg_nc_v4(rel_row + st);
-    w[4 * v] = x.x;
-    w[4 * v + 1] = x.y;
-    w[4 * v + 2] = x.z;
-    w[4 * v + 3] = x.w;
-  }
-}
-
-// x[i] += log2(e) * bias of column i of chunk cc, from the window above: column i has distance
-// dtop - 32 cc - i = element (off + 31 - i) of the window, off = (dtop - 32 cc - 31) mod 8; the
-// window is shifted by off elements with selects and a byte permute (no shared memory).
-__device__ __forceinline__ void add_bias_window(const uint32_t (&w)[20], int dtop, int cc,
-                                                float (&x)[32]) {
-  const int off = (dtop - 32 * cc - 31) & 7;
-  const int q = off >> 1;  // whole words to skip
-  uint32_t t2[17];
-#pragma unroll
-  for (int k = 0; k < 17; ++k)
-    t2[k] = (q & 2) ? ((q & 1) ? w[k + 3] : w[k + 2]) : ((q & 1) ? w[k + 1] : w[k]);
-  const uint32_t sel = (off & 1) ? 0x5432u : 0x3210u;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int j = 31 - i;  // element j of the shifted window
-    const uint32_t pr = __byte_perm(t2[j >> 1], t2[(j >> 1) + 1], sel);
-    x[i] += __uint_as_float((j & 1) ? (pr & 0xffff0000u) : (pr << 16)) * kLog2e;
-  }
-}
-
 __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr) {
   const uint64_t qd = sdesc_sw128(q_addr, 16, 1024);
   const uint64_t kd = sdesc_sw128(k_addr, 16, 1024);
