@@ -338,6 +338,21 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   int64_t max_sq = p->max_seqlen_q > 0 ? p->max_seqlen_q : p->total_q;
   if (max_sq > p->total_q) max_sq = p->total_q;
   int64_t slots = (max_sq + rows_per_cta - 1) / rows_per_cta;
+  // Query slots per (head slot, sequence): enough for the average sequence (longer ones
+  // stride over their tiles, CTA z taking tiles z, z + slots, ... heaviest first, which pairs
+  // heavy with light tiles), but at least four waves of CTAs.  With one sequence (or equal
+  // lengths) this is the longest sequence's tile count: one tile set per CTA.
+  {
+    const int64_t avg_sq = (p->total_q + p->batch - 1) / p->batch;
+    const int64_t avg_slots = (avg_sq + rows_per_cta - 1) / rows_per_cta;
+    int sms = 148;
+    if ((rc = sm_count(&sms))) return rc;
+    const int64_t head_slots = a.pair_heads ? p->n_heads / 2 : p->n_heads;
+    const int64_t per_z = head_slots * p->batch;
+    const int64_t min_slots = (4LL * sms + per_z - 1) / per_z;
+    int64_t want = avg_slots > min_slots ? avg_slots : min_slots;
+    if (want < slots) slots = want;
+  }
   if (slots < 1) slots = 1;
   if (slots > 65535) slots = 65535;
   cudaError_t e = ifa4::launch_prefill_sm100(a, tq, tk, tv, static_cast<int>(slots),
