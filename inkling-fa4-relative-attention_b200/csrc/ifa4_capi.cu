@@ -379,12 +379,21 @@ static int decode_plan(const IFA4DecodeParams* p, int* num_splits, int* chunk_le
     return fail(IFA4_ERR_INVALID_ARGUMENT, "decode: chunk_len must be a multiple of 64");
   if (splits < 0) return fail(IFA4_ERR_INVALID_ARGUMENT, "decode: num_splits < 0");
   if (chunk == 0) {
+    // 2048-key chunks balance ragged lengths across CTAs; only when they would leave SMs idle
+    // (small batches) are they shortened, to at most one CTA per SM (measured on B200 at batch 1
+    // and 32k keys: 18 x 1856-key chunks (144 CTAs) 36 us, 19 x 1728 (152: four SMs run two)
+    // 40 us, 64 x 256 (two CTA waves, each paying the pipeline start) 46 us).
     int sms = 148;
     int rc = sm_count(&sms);
     if (rc) return rc;
     const int64_t ctas_per_split = static_cast<int64_t>(p->batch) * p->kv_heads * head_blocks;
     chunk = 2048;
-    while (chunk > 256 && ctas_per_split * ((max_sk + chunk - 1) / chunk) < 4LL * sms) chunk /= 2;
+    if (ctas_per_split * ((max_sk + chunk - 1) / chunk) < sms) {
+      const int64_t want_splits = sms / ctas_per_split > 0 ? sms / ctas_per_split : 1;
+      int64_t c = (max_sk + want_splits - 1) / want_splits;
+      c = (c + 63) / 64 * 64;
+      chunk = static_cast<int>(c < 64 ? 64 : (c > 2048 ? 2048 : c));
+    }
   }
   if (splits == 0) {
     int64_t s = (max_sk + chunk - 1) / chunk;
