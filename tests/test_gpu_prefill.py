@@ -178,3 +178,25 @@ def test_window_row_without_keys_is_zero_in_default_config():
     out = run_prefill(c, causal_align="bottom_right", window_size=(0, 0))
     want = oracle_full(c, 1 / 128, window_left=0, causal_align="bottom_right")
     assert_close(np32(out), want)
+
+
+@pytest.mark.parametrize("jump", [1000, 1024, 1056, 1090, 1130])
+def test_running_max_growth_inside_interior_tiles(jump):
+    """Keys from `jump` on are scaled 60x, so for rows far past them the scores jump by much
+    more than the rescale threshold inside an interior (unmasked, unbiased) KV tile, at the 32-
+    column chunk position the offset selects: the single-pass softmax must correct its running
+    max, sum, stored P and O there."""
+    from inkling_fa4.workloads import Case
+    c = make_case([2048, 1500], [2048, 1500], 4, 2, 128, seed=jump)
+    k = c.k.float()
+    k[jump:2048] *= 60.0
+    k[2048 + jump // 2:] *= 60.0
+    c = Case(q=c.q, k=k.to(torch.bfloat16), v=c.v, rel=c.rel, cu_q=c.cu_q, cu_k=c.cu_k,
+             seqlens_q=c.seqlens_q, seqlens_k=c.seqlens_k, rel_extent=128)
+    c = to_dev(c)
+    toks, want = oracle_rows(c, 48, list(range(4)), 1 / 128, seed=jump)
+    from inkling_fa4 import _ops
+    for tc in (1, 3):  # all-SFU and FMA-pipe exponential variants
+        out = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, c.max_q, c.max_k, 128,
+                           tile_config=tc)
+        assert_close(np32(out)[toks], want, what=f"tile_config {tc}")
