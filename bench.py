@@ -12,7 +12,8 @@ excluded.  Scaling is weak: every rank owns an independent 32k sequence (work sh
 sequence / KV-head group with no data-path collective); ``value`` = all ranks' FLOPs / the
 slowest rank's time.
 
-Secondary objects in the same JSON line: the sliding-window variant (window 4096), batched
+Secondary objects in the same JSON line: the sliding-window variant (window 4096), the backward,
+the rel_logits producer for the headline shape (GB/s against HBM), batched
 decode (GB/s and us/step against HBM), the end-to-end number through the
 public API with host buffers (``e2e``), the CPU baseline (the oracle on host cores, bounded
 sample) and SM clocks sampled during the timed region.
@@ -250,10 +251,12 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-window", action="store_true")
     ap.add_argument("--no-backward", action="store_true")
+    ap.add_argument("--no-rel-logits", action="store_true")
     ap.add_argument("--extra-configs", action="store_true",
                     help="also time BASELINE configs 2 (ragged) and 4 (chunked)")
-    ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
-                    help="prefill: headline + window only; decode: decode only (profiling runs)")
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "rel_logits"], default="all",
+                    help="prefill: headline + window only; decode: decode only; rel_logits: the "
+                         "producer only (profiling runs)")
     ap.add_argument("--prefill-seq", type=int, default=SEQ,
                     help="sequence length of the prefill workload (32768 = BASELINE config 3)")
     ap.add_argument("--tile-config", type=int, default=0,
@@ -262,9 +265,11 @@ def main():
                     help="decode batch (128 = BASELINE config 5)")
     args = ap.parse_args()
     if args.only == "prefill":
-        args.no_decode = True
+        args.no_decode = args.no_rel_logits = True
     if args.only == "decode":
-        args.no_e2e = args.no_window = args.no_backward = True
+        args.no_e2e = args.no_window = args.no_backward = args.no_rel_logits = True
+    if args.only == "rel_logits":
+        args.no_e2e = args.no_window = args.no_backward = args.no_decode = True
     if args.warmup < 3:
         args.warmup = 3
 
@@ -317,7 +322,7 @@ def main():
     except Exception:
         pass
     sampler = ClockSampler(uuids) if rank == 0 else None
-    if args.only == "decode":
+    if args.only in ("decode", "rel_logits"):
         ms, clocks = float("nan"), None
     else:
         if sampler:
@@ -472,6 +477,43 @@ def main():
                        "rel_attn_bwd_dq_kernel (3 launches per step)",
             "gpu_launches": 3 * bsteps}
         del bout, blse, bdout, bws, bufs
+
+    # ---------------- rel_logits producer for the headline shape (the step before the path)
+    if not args.no_rel_logits:
+        from inkling_fa4 import inkling_rel_logits
+
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(2000 + rank)
+        rr = torch.randn((S, HQ, 16), generator=gen, device=dev).to(torch.bfloat16)
+        rw = (0.5 * torch.randn((HQ, 16, R), generator=gen, device=dev)).to(torch.bfloat16)
+        rout = torch.empty((S, HQ, R), dtype=torch.bfloat16, device=dev)
+
+        def rl_step():
+            return inkling_rel_logits(rr, rw, alpha=0.1, nf=4096.0, out=rout)
+
+        rms = timed(rl_step, args.steps, args.warmup, stream, dist, barrier)
+        rbytes = rr.numel() * 2 + rw.numel() * 2 + rout.numel() * 2
+        rgbs = rbytes * args.steps / (rms / 1e3) / 1e9
+        # Write-stream reference on the same box: torch's fill_ of the same output buffer, same
+        # protocol (the producer's traffic is 89 % writes; a plain write stream reaches well
+        # below the read+write copy peak).
+        fms = timed(lambda: rout.fill_(1.0), args.steps, args.warmup, stream, dist, barrier)
+        fill_gbs = rout.numel() * 2 * args.steps / (fms / 1e3) / 1e9
+        write_gbs = rout.numel() * 2 * args.steps / (rms / 1e3) / 1e9
+        result["rel_logits32k"] = {
+            "value": world * rgbs, "unit": "GB/s", "us_per_step": rms * 1e3 / args.steps,
+            "config": {"workload": "rel_logits_32k_h32_r128", "tokens": S, "n_heads": HQ,
+                       "d_rel": 16, "rel_extent": R, "weight": "per head", "alpha": 0.1,
+                       "nf": 4096.0, "bytes_per_step_per_gpu": rbytes,
+                       "l2": "working set 302 MB > 126 MB L2 (the 268 MB output streams out "
+                             "every step)"},
+            "roofline": {"bound": "hbm", "achieved": rgbs, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": rgbs / peaks["hbm_gbs"],
+                         "peak_source": f"hbm_gbs of {peak_kind}",
+                         "write_gbs": write_gbs, "fill_gbs_same_buffer": fill_gbs,
+                         "write_frac_of_fill": write_gbs / fill_gbs},
+            "kernel": "rel_logits_kernel (1 launch per step)", "gpu_launches": args.steps}
+        del rr, rw, rout
     del c
     torch.cuda.empty_cache()
 

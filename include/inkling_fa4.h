@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define IFA4_ABI_VERSION 4
+#define IFA4_ABI_VERSION 5
 
 enum {
   IFA4_OK = 0,
@@ -238,6 +238,43 @@ int ifa4_backward_workspace_size(const IFA4BackwardParams* params, size_t* bytes
 int ifa4_backward_launch(const IFA4BackwardParams* params, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* rel_logits producer: the step before the attention in the Inkling layer (RelLogitsProj plus
+ * the log-tau scaling, outputs/architecture.md:51-64 of the reference repository, which holds
+ * only that diagram and no code for it), fused into one kernel:
+ *   rel[t, h, e] = bf16( tau(pos_t) * sum_{j < 16} r[t, h, j] * W_h[j, e] ),  0 <= e < rel_extent
+ *   tau(p) = 1 + alpha * log(max((p + 1) / nf, 1))        (alpha = 0: tau = 1 exactly)
+ * with fp32 products and sums (tensor cores) and one rounding to bf16.  pos_t is the token's
+ * position in its sequence: t - cu_seqlens_q[b] for the sequence b holding t, plus
+ * (len_k(b) - len_q(b)) when cu_seqlens_k is given (queries are the last len_q of len_k
+ * positions, as in chunked prefill and decode).  cu_seqlens_q NULL means one sequence.
+ * r    [total_q, n_heads, 16] bf16: 16-byte aligned base, strides multiples of 8 elements
+ *      (a slice of a merged projection output qualifies).
+ * W    [16, rel_extent] shared by all heads (weight_stride_h = 0) or [n_heads, 16, rel_extent]
+ *      bf16: 16-byte aligned, last dimension contiguous, strides multiples of 8 elements.
+ * rel  [total_q, n_heads, >= rel_extent] bf16: 16-byte aligned, strides multiples of 8
+ *      elements; columns [0, rel_extent) written.  rel_extent must be a multiple of 8.
+ * The kernel's one wait per tile is bounded like the others (status bit 5). */
+typedef struct IFA4RelLogitsParams {
+  const void* r;
+  const void* weight;
+  void* rel;
+  const int32_t* cu_seqlens_q;  /* optional, int32 [batch + 1] on the device */
+  const int32_t* cu_seqlens_k;  /* optional, int32 [batch + 1] on the device */
+  int64_t r_stride_t, r_stride_h;
+  int64_t weight_stride_h, weight_stride_j;
+  int64_t rel_stride_t, rel_stride_h;
+  int64_t total_q;
+  int32_t batch;      /* number of sequences (1 when cu_seqlens_q is NULL) */
+  int32_t n_heads;
+  int32_t d_rel;      /* must be 16 */
+  int32_t rel_extent;
+  int32_t dtype;
+  float alpha;
+  float nf;           /* > 0 */
+} IFA4RelLogitsParams;
+
+int ifa4_rel_logits_launch(const IFA4RelLogitsParams* params, void* stream);
+
 /* Self-test of the failure detection (test hook; the reference has no counterpart): launches
  * on `stream` a kernel whose barrier wait can never complete, so the kernels' bounded-wait path
  * runs out after timeout_ns (0 < timeout_ns <= 1e9).  Afterwards the status word holds exactly
@@ -250,7 +287,7 @@ int ifa4_selftest_bounded_wait(int64_t timeout_ns, void* stream);
 /* Reads (and optionally clears) the library's device status word on `stream`, blocking the
  * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on
  * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode, bit 2 backward, bits 3-4
- * ifa4_selftest_bounded_wait.  Test hook; the
+ * ifa4_selftest_bounded_wait, bit 5 rel_logits producer.  Test hook; the
  * reference has no counterpart. */
 int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out);
 

@@ -706,6 +706,112 @@ int ifa4_backward_launch(const IFA4BackwardParams* p, void* workspace, size_t wo
   return IFA4_OK;
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// rel_logits producer
+// ---------------------------------------------------------------------------------------
+namespace {
+int validate_rel_logits(const IFA4RelLogitsParams* p) {
+  if (p == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "rel_logits: params is NULL");
+  if (p->dtype != IFA4_DTYPE_BF16)
+    return fail(IFA4_ERR_UNSUPPORTED, "rel_logits: dtype %d unsupported (bf16 only)", p->dtype);
+  if (p->d_rel != 16)
+    return fail(IFA4_ERR_UNSUPPORTED, "rel_logits: d_rel %d unsupported (16 only)", p->d_rel);
+  if (p->total_q < 0 || p->n_heads <= 0 || p->rel_extent <= 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT,
+                "rel_logits: total_q must be >= 0, n_heads and rel_extent > 0");
+  if (p->rel_extent % 8 != 0)
+    return fail(IFA4_ERR_UNSUPPORTED, "rel_logits: rel_extent %d is not a multiple of 8",
+                p->rel_extent);
+  if (p->total_q > 2147483647LL - 256)
+    return fail(IFA4_ERR_UNSUPPORTED, "rel_logits: total_q beyond 2^31 - 256");
+  if (static_cast<int64_t>(p->n_heads) * ((p->rel_extent + 127) / 128) > (1LL << 30))
+    return fail(IFA4_ERR_UNSUPPORTED, "rel_logits: n_heads x rel_extent / 128 beyond 2^30");
+  if (!(p->nf > 0.f) || !(p->nf < 3.0e38f) || !(p->alpha > -3.0e38f && p->alpha < 3.0e38f))
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "rel_logits: nf must be finite and > 0, alpha finite");
+  if (p->cu_seqlens_k != nullptr && p->cu_seqlens_q == nullptr)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "rel_logits: cu_seqlens_k given without cu_seqlens_q");
+  if (p->cu_seqlens_q != nullptr && p->batch <= 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "rel_logits: batch must be > 0 with cu_seqlens_q");
+  if (p->total_q == 0) return IFA4_OK;
+  if (!p->r || !p->weight || !p->rel)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "rel_logits: null tensor pointer");
+  if (!aligned16(p->r) || !aligned16(p->rel))
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "rel_logits: r and rel must be 16-byte aligned");
+  const int64_t s8[] = {p->r_stride_t, p->r_stride_h, p->rel_stride_t, p->rel_stride_h};
+  for (int64_t s : s8)
+    if (s <= 0 || (s % 8) != 0)
+      return fail(IFA4_ERR_INVALID_ARGUMENT,
+                  "rel_logits: r and rel token/head strides must be positive multiples of 8 "
+                  "elements");
+  if (!aligned16(p->weight) || p->weight_stride_h < 0 || p->weight_stride_j <= 0 ||
+      p->weight_stride_h % 8 != 0 || p->weight_stride_j % 8 != 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT,
+                "rel_logits: weight must be 16-byte aligned with head stride a multiple of 8 "
+                "elements (0 = shared) and row stride a positive multiple of 8");
+  return IFA4_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ifa4_rel_logits_launch(const IFA4RelLogitsParams* p, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = validate_rel_logits(p);
+  if (rc) return rc;
+  if (p->total_q == 0) return IFA4_OK;
+  int* status = nullptr;
+  if ((rc = device_status_ptr(&status))) return rc;
+  int sms = 0;
+  if ((rc = sm_count(&sms))) return rc;
+
+  EncodeTiledFn fn;
+  if ((rc = get_encode_fn(&fn))) return rc;
+  CUtensorMap trel;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(p->rel_extent),
+                        static_cast<cuuint64_t>(p->n_heads), static_cast<cuuint64_t>(p->total_q)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(p->rel_stride_h) * 2,
+                           static_cast<cuuint64_t>(p->rel_stride_t) * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(&trel, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, p->rel, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(IFA4_ERR_UNSUPPORTED,
+                "cuTensorMapEncodeTiled(rel) failed with CUresult %d (total_q=%lld heads=%d "
+                "rel_extent=%d stride_t=%lld stride_h=%lld)",
+                static_cast<int>(r), static_cast<long long>(p->total_q), p->n_heads,
+                p->rel_extent, static_cast<long long>(p->rel_stride_t),
+                static_cast<long long>(p->rel_stride_h));
+
+  ifa4::RelLogitsKernelArgs a{};
+  a.r = static_cast<const uint16_t*>(p->r);
+  a.w = static_cast<const uint16_t*>(p->weight);
+  a.cu_q = p->cu_seqlens_q;
+  a.cu_k = p->cu_seqlens_q != nullptr ? p->cu_seqlens_k : nullptr;
+  a.r_st = p->r_stride_t;
+  a.r_sh = p->r_stride_h;
+  a.w_sh = p->weight_stride_h;
+  a.w_sj = p->weight_stride_j;
+  a.total_q = p->total_q;
+  a.batch = p->cu_seqlens_q != nullptr ? p->batch : 1;
+  a.n_heads = p->n_heads;
+  a.rel_extent = p->rel_extent;
+  a.col_blocks = (p->rel_extent + 127) / 128;
+  a.head_quads = (p->n_heads + 3) / 4;
+  a.units = ((p->total_q + 127) / 128) * static_cast<int64_t>(a.head_quads) * a.col_blocks;
+  a.alpha = p->alpha;
+  a.nf = p->nf;
+  a.status = status;
+  const int64_t cap = static_cast<int64_t>(sms) * ifa4::kRelLogitsCtasPerSm;
+  const int grid = static_cast<int>(a.units < cap ? a.units : cap);
+  cudaError_t e = ifa4::launch_rel_logits_sm100(a, trel, grid, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rel_logits launch");
+  return IFA4_OK;
+}
+
 int ifa4_selftest_bounded_wait(int64_t timeout_ns, void* stream) {
   g_last_error[0] = '\0';
   if (timeout_ns <= 0 || timeout_ns > 1000000000LL)

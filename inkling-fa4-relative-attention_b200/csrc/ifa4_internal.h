@@ -15,6 +15,7 @@ constexpr int kStatusDecodeTimeout = 2;
 constexpr int kStatusBackwardTimeout = 4;
 constexpr int kStatusSelfTestTimeout = 8;   // ifa4_selftest_bounded_wait, warp 0
 constexpr int kStatusSelfTestOwnTimeout = 16;  // ifa4_selftest_bounded_wait, warp 1 (must not be set)
+constexpr int kStatusRelLogitsTimeout = 32;
 
 struct PrefillKernelArgs {
   const uint16_t* rel;       // bf16 bits
@@ -116,6 +117,29 @@ struct BackwardKernelArgs {
   int bias_vec;              // rel 16-byte aligned and rel_extent % 8 == 0 (vector bias windows)
   int* status;
 };
+
+// rel_logits producer: rel[t, h, e] = bf16(tau(pos_t) * sum_j r[t, h, j] * W_h[j, e]).
+struct RelLogitsKernelArgs {
+  const uint16_t* r;         // bf16 bits, r[t * r_st + h * r_sh + j], j < 16
+  const uint16_t* w;         // bf16 bits, W_h[j, e] at w[h * w_sh + j * w_sj + e]
+  const int32_t* cu_q;       // optional (null: one sequence)
+  const int32_t* cu_k;       // optional (null: positions start at 0)
+  long long r_st, r_sh, w_sh, w_sj;
+  long long total_q;
+  long long units;           // quads: token tiles x head_quads x col_blocks
+  int batch, n_heads, rel_extent;
+  int head_quads;            // ceil(n_heads / 4)
+  int col_blocks;            // ceil(rel_extent / 128)
+  float alpha, nf;
+  int* status;
+};
+
+// Grid of `grid` CTAs (up to kRelLogitsCtasPerSm per SM) striding over args.units quads of
+// 128 tokens x 4 heads x 128 columns; rel written through tm_rel ({rel_extent, n_heads, total_q},
+// 64 x 1 x 128 boxes, 128-byte swizzle).
+cudaError_t launch_rel_logits_sm100(const RelLogitsKernelArgs& args, const CUtensorMap& tm_rel,
+                                    int grid, cudaStream_t stream);
+constexpr int kRelLogitsCtasPerSm = 4;
 
 // Prep (Delta, zeroed d rel band), dK/dV (+ d rel) and dQ kernels, in that order on `stream`.
 cudaError_t launch_backward_sm100(const BackwardKernelArgs& args, const CUtensorMap& tm_q,

@@ -19,7 +19,7 @@ IFA4_ERR_DEVICE_TIMEOUT = -5
 IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0
-ABI_VERSION = 4
+ABI_VERSION = 5
 NOALLOC_DECODE_SCRATCH_BYTES = 16 * 1024 * 1024
 
 EXPORTED_SYMBOLS = (
@@ -29,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "ifa4_decode_workspace_size",
     "ifa4_backward_launch",
     "ifa4_backward_workspace_size",
+    "ifa4_rel_logits_launch",
     "ifa4_read_device_status",
     "ifa4_selftest_bounded_wait",
     "ifa4_prefill_tile_config_name",
@@ -96,6 +97,18 @@ class BackwardParams(ctypes.Structure):
         [("softmax_scale", ctypes.c_float)]
 
 
+class RelLogitsParams(ctypes.Structure):
+    """Mirror of ``IFA4RelLogitsParams``."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("r", "weight", "rel", "cu_seqlens_q",
+                                               "cu_seqlens_k")] + \
+        [("r_stride_t", ctypes.c_int64), ("r_stride_h", ctypes.c_int64),
+         ("weight_stride_h", ctypes.c_int64), ("weight_stride_j", ctypes.c_int64),
+         ("rel_stride_t", ctypes.c_int64), ("rel_stride_h", ctypes.c_int64),
+         ("total_q", ctypes.c_int64)] + \
+        [(n, ctypes.c_int32) for n in ("batch", "n_heads", "d_rel", "rel_extent", "dtype")] + \
+        [("alpha", ctypes.c_float), ("nf", ctypes.c_float)]
+
+
 class Ifa4Error(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"inkling_fa4 error {code}: {message}")
@@ -129,6 +142,8 @@ def lib() -> ctypes.CDLL:
     L.ifa4_backward_launch.restype = ctypes.c_int
     L.ifa4_backward_workspace_size.argtypes = [ctypes.POINTER(BackwardParams), ctypes.POINTER(sz)]
     L.ifa4_backward_workspace_size.restype = ctypes.c_int
+    L.ifa4_rel_logits_launch.argtypes = [ctypes.POINTER(RelLogitsParams), vp]
+    L.ifa4_rel_logits_launch.restype = ctypes.c_int
     L.ifa4_selftest_bounded_wait.argtypes = [ctypes.c_int64, vp]
     L.ifa4_selftest_bounded_wait.restype = ctypes.c_int
     L.ifa4_read_device_status.argtypes = [vp, i32, ctypes.POINTER(i32)]

@@ -19,7 +19,8 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(ROOT, "csrc")
 OUT = os.path.join(PKG_DIR, "_lib", "libinkling_fa4.so")
-SOURCES = ["ifa4_capi.cu", "ifa4_prefill_sm100.cu", "ifa4_decode_sm100.cu", "ifa4_backward_sm100.cu"]
+SOURCES = ["ifa4_capi.cu", "ifa4_prefill_sm100.cu", "ifa4_decode_sm100.cu", "ifa4_backward_sm100.cu",
+           "ifa4_rel_logits_sm100.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

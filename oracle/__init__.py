@@ -1,4 +1,5 @@
-"""CPU oracle (test infrastructure only): see ``oracle/rel_attn_oracle.py``."""
+"""CPU oracle (test infrastructure only): see ``oracle/rel_attn_oracle.py`` (attention) and
+``oracle/rel_logits_oracle.py`` (rel_logits producer)."""
 from .rel_attn_oracle import (  # noqa: F401
     rel_attn,
     rel_attn_rows,
@@ -10,3 +11,4 @@ from .rel_attn_oracle import (  # noqa: F401
     rel_attn_rows_torch,
     rel_attn_grads_torch,
 )
+from .rel_logits_oracle import token_positions, log_tau, rel_logits_proj  # noqa: F401

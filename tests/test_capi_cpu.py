@@ -47,7 +47,9 @@ def test_abi_version_and_tile_name():
 
 
 @pytest.mark.parametrize("cls,cname", [(_lib.PrefillParams, "IFA4PrefillParams"),
-                                       (_lib.DecodeParams, "IFA4DecodeParams")])
+                                       (_lib.DecodeParams, "IFA4DecodeParams"),
+                                       (_lib.BackwardParams, "IFA4BackwardParams"),
+                                       (_lib.RelLogitsParams, "IFA4RelLogitsParams")])
 def test_struct_layout_matches_header(cls, cname):
     fields = [f[0] for f in cls._fields_]
     src = "#include <stdio.h>\n#include <stddef.h>\n#include \"inkling_fa4.h\"\nint main(){\n"
