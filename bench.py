@@ -511,7 +511,11 @@ def main():
                          "unit": "GB/s", "frac": rgbs / peaks["hbm_gbs"],
                          "peak_source": f"hbm_gbs of {peak_kind}",
                          "write_gbs": write_gbs, "fill_gbs_same_buffer": fill_gbs,
-                         "write_frac_of_fill": write_gbs / fill_gbs},
+                         "write_frac_of_fill": write_gbs / fill_gbs,
+                         "traffic": (profile_traffic("rel_logits_32k_ncu.md")
+                                     if S == SEQ else None),
+                         "traffic_note": "one cold ncu launch: reads + writes performed before "
+                                         "it ended (54 MB of output still dirty in L2)"},
             "kernel": "rel_logits_kernel (1 launch per step)", "gpu_launches": args.steps}
         del rr, rw, rout
     del c
