@@ -510,16 +510,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
           tmem_wait_ld();
+          // columns 0..3 start four chains; 4..123 in steps of 8 (a step at column 28 of a
+          // 32-column array continues into the next array); then 124..127
           float mA = __uint_as_float(r[0][0]), mB = __uint_as_float(r[0][1]);
           float mC = __uint_as_float(r[0][2]), mD = __uint_as_float(r[0][3]);
 #pragma unroll
-          for (int c = 4; c < 128; c += 8) {
-            const uint32_t* v = &r[c >> 5][c & 31];
-            mA = fmax3(mA, __uint_as_float(v[0]), __uint_as_float(v[1]));
-            mB = fmax3(mB, __uint_as_float(v[2]), __uint_as_float(v[3]));
-            mC = fmax3(mC, __uint_as_float(v[4]), __uint_as_float(v[5]));
-            mD = fmax3(mD, __uint_as_float(v[6]), __uint_as_float(v[7]));
+          for (int c = 4; c < 124; c += 8) {
+            const int cc = c >> 5, i = c & 31;
+            if (i + 7 < 32) {
+              mA = fmax3(mA, __uint_as_float(r[cc][i]), __uint_as_float(r[cc][i + 1]));
+              mB = fmax3(mB, __uint_as_float(r[cc][i + 2]), __uint_as_float(r[cc][i + 3]));
+              mC = fmax3(mC, __uint_as_float(r[cc][i + 4]), __uint_as_float(r[cc][i + 5]));
+              mD = fmax3(mD, __uint_as_float(r[cc][i + 6]), __uint_as_float(r[cc][i + 7]));
+            } else {
+              mA = fmax3(mA, __uint_as_float(r[cc][28]), __uint_as_float(r[cc][29]));
+              mB = fmax3(mB, __uint_as_float(r[cc][30]), __uint_as_float(r[cc][31]));
+              mC = fmax3(mC, __uint_as_float(r[cc + 1][0]), __uint_as_float(r[cc + 1][1]));
+              mD = fmax3(mD, __uint_as_float(r[cc + 1][2]), __uint_as_float(r[cc + 1][3]));
+            }
           }
+          mA = fmax3(mA, __uint_as_float(r[3][28]), __uint_as_float(r[3][29]));
+          mB = fmax3(mB, __uint_as_float(r[3][30]), __uint_as_float(r[3][31]));
           mul = a.scale_log2;
           m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
         } else {
@@ -576,10 +587,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             float m0 = x[0], m1 = x[1];
 #pragma unroll
-            for (int i = 2; i < 32; i += 4) {
+            for (int i = 2; i < 30; i += 4) {  // columns 2..29, then 30 and 31
               m0 = fmax3(m0, x[i], x[i + 1]);
               m1 = fmax3(m1, x[i + 2], x[i + 3]);
             }
+            m0 = fmax3(m0, x[30], x[31]);
             mx = fmax3(mx, m0, m1);
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
