@@ -252,6 +252,8 @@ def main():
     ap.add_argument("--no-window", action="store_true")
     ap.add_argument("--no-backward", action="store_true")
     ap.add_argument("--no-rel-logits", action="store_true")
+    ap.add_argument("--no-shard", action="store_true",
+                    help="skip the head-sharded single-sequence leg (N > 1 only)")
     ap.add_argument("--extra-configs", action="store_true",
                     help="also time BASELINE configs 2 (ragged) and 4 (chunked)")
     ap.add_argument("--only", choices=["all", "prefill", "decode", "rel_logits"], default="all",
@@ -265,11 +267,13 @@ def main():
                     help="decode batch (128 = BASELINE config 5)")
     args = ap.parse_args()
     if args.only == "prefill":
-        args.no_decode = args.no_rel_logits = True
+        args.no_decode = args.no_rel_logits = args.no_shard = True
     if args.only == "decode":
         args.no_e2e = args.no_window = args.no_backward = args.no_rel_logits = True
+        args.no_shard = True
     if args.only == "rel_logits":
         args.no_e2e = args.no_window = args.no_backward = args.no_decode = True
+        args.no_shard = True
     if args.warmup < 3:
         args.warmup = 3
 
@@ -520,6 +524,36 @@ def main():
         del rr, rw, rout
     del c
     torch.cuda.empty_cache()
+
+    # ---------------- one 32k sequence sharded by KV-head group over the ranks (N > 1 only)
+    # Strong scaling of a single call: rank r runs the heads of kv groups [r*8/N, (r+1)*8/N) of
+    # the same sequence (head-slice views, no copies), timed without and with the NCCL
+    # all-gather that assembles the [T, 32, 128] output on every rank.
+    if world > 1 and not args.no_shard and HKV % world == 0:
+        from inkling_fa4.sharding import gather_heads, head_shard, shard_tensors
+
+        sc = config_long(device=dev, seed=0, seq=S, gen_device=dev)  # same sequence on all ranks
+        sh = head_shard(HQ, HKV, world, rank)
+        q_s, k_s, v_s, rel_s = shard_tensors(sh, sc.q, sc.k, sc.v, sc.rel)
+        shard_step = lambda: inkling_fa4_rel_attention_triton(q_s, k_s, v_s, rel_s, sc.cu_q,
+                                                               sc.cu_k, S, S, R)
+        gather_step = lambda: gather_heads(shard_step(), world)
+        ms_ng = timed(shard_step, args.steps, args.warmup, stream, dist, barrier)
+        ms_g = timed(gather_step, args.steps, args.warmup, stream, dist, barrier)
+        full_flops = 4 * D * HQ * visible_pairs_causal(S)
+        result["head_sharded32k"] = {
+            "unit": "TFLOP/s", "scaling": "strong",
+            "value_no_gather": full_flops * args.steps / (ms_ng / 1e3) / 1e12,
+            "value_with_gather": full_flops * args.steps / (ms_g / 1e3) / 1e12,
+            "ms_per_step_no_gather": ms_ng / args.steps,
+            "ms_per_step_with_gather": ms_g / args.steps,
+            "config": {"workload": "causal32k_gqa32_8_d128_rel128, one sequence",
+                       "heads_per_rank": sh.n_q, "kv_heads_per_rank": sh.n_kv,
+                       "collective": "one NCCL all_gather_into_tensor of the output heads "
+                                     f"({S * HQ * D * 2 >> 20} MB assembled per step)"},
+            "gpu_launches": args.steps}
+        del sc, q_s, k_s, v_s, rel_s
+        torch.cuda.empty_cache()
 
     # ---------------- ragged (config 2) and chunked (config 4) prefill, on request
     if args.extra_configs:
