@@ -30,6 +30,8 @@ struct PrefillKernelArgs {
                              // each row loads its bias with 16-byte vectors
   int pair_heads;            // 1: the CTA's two sub-tiles are two heads at the same rows
                              // 0: the CTA's two sub-tiles are consecutive 128-row blocks
+  int q_fastest;             // grid (query slots, head slots, sequences) rather than
+                             // (head slots, sequences, query slots)
   float scale_log2;          // softmax_scale * log2(e)
   float* lse;                // optional natural-log LSE, [h * lse_sh + token * lse_st]
   long long lse_sh, lse_st;

@@ -134,7 +134,8 @@ __device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_
                                               Bars* bars, const CUtensorMap* tm_q,
                                               const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                               int hslot, int b, int q_start, int sq, int sk,
-                                              int n_qt, int lane, const AbortCtx& ab) {
+                                              int n_qt, int slot0, int slot_step, int lane,
+                                              const AbortCtx& ab) {
   uint32_t qc = 0, kc = 0, vc = 0;
   const uint64_t pol_kv = l2_policy_evict_last();
   const uint64_t pol_q = l2_policy_evict_first();
@@ -143,7 +144,7 @@ __device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_
   const int page_mask = (1 << a.page_shift) - 1;
   const int32_t* bt = a.block_table + static_cast<long long>(b) * a.bt_stride;
   bool ok = true;
-  for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+  for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
     const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
     if (t.n_kv == 0) continue;
     if (!(ok = mbar_wait_warp(&bars->q_empty, (qc & 1) ^ 1, ab))) break;
@@ -271,15 +272,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int hslot = blockIdx.x;
-  const int b = blockIdx.y;
+  // Grid (query slots, head slots, sequences) when one query tile's key range over all KV
+  // heads outgrows L2: the query slots of one head slot then launch together, so the CTAs
+  // resident at one time read the K/V of few KV heads and those tiles stay in L2.  Otherwise
+  // (head slots, sequences, query slots), which spreads a ragged batch's sequences over the
+  // first waves.
+  const int hslot = a.q_fastest ? blockIdx.y : blockIdx.x;
+  const int b = a.q_fastest ? blockIdx.z : blockIdx.y;
+  const int slot0 = a.q_fastest ? blockIdx.x : blockIdx.z;
+  const int slot_step = a.q_fastest ? gridDim.x : gridDim.z;
   const int q_start = a.cu_q[b];
   const int sq = a.cu_q[b + 1] - q_start;
   const int k_start = a.cu_k[b];
   const int sk = a.cu_k[b + 1] - k_start;
   const int rows_per_cta = a.pair_heads ? kBM : 2 * kBM;
   const int n_qt = (sq + rows_per_cta - 1) / rows_per_cta;
-  if (static_cast<int>(blockIdx.z) >= n_qt) return;  // uniform over the CTA: nothing to do
+  if (slot0 >= n_qt) return;  // uniform over the CTA: nothing to do
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -314,14 +322,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
   if (warp < 4) {
    if (kPaged && warp == 0) {
-    produce_paged(a, smem, bars, &tm_q, &tm_k, &tm_v, hslot, b, q_start, sq, sk, n_qt, lane, ab);
+    produce_paged(a, smem, bars, &tm_q, &tm_k, &tm_v, hslot, b, q_start, sq, sk, n_qt, slot0,
+                  slot_step, lane, ab);
    } else if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t qc = 0, kc = 0, vc = 0;
       const uint64_t pol_kv = l2_policy_evict_last();
       const uint64_t pol_q = l2_policy_evict_first();
-      for (int slot = blockIdx.z; slot < n_qt; slot += gridDim.z) {
+      for (int slot = slot0; slot < n_qt; slot += slot_step) {
         const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
         if (t.n_kv == 0) continue;
         if (!mbar_wait(&bars->q_empty, (qc & 1) ^ 1, ab)) break;
@@ -373,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t k_addr = smem_u32(smem + kSmemK);
       const uint32_t v_addr = smem_u32(smem + kSmemV);
       bool ok = true;
-      for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+      for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
         const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
         if (t.n_kv == 0) continue;
         if (!(ok = mbar_wait(&bars->q_full, qc & 1, ab))) break;
@@ -445,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int bs = a.align_bottom_right ? sk - sq : sq - sk;
     uint32_t pc = 0, oc = 0;
     bool ok = true;
-    for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+    for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
       const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
       const int qi = t.row0[s] + row;
       const bool row_valid = qi < sq;
@@ -792,7 +801,8 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
                                  int q_slots, int tile_config, int max_seqlen_q,
                                  cudaStream_t stream) {
   const int head_slots = args.pair_heads ? args.n_heads / 2 : args.n_heads;
-  dim3 grid(head_slots, args.batch, q_slots);
+  dim3 grid = args.q_fastest ? dim3(q_slots, head_slots, args.batch)
+                             : dim3(head_slots, args.batch, q_slots);
   if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return cudaErrorInvalidValue;
   int emu = kVariants[tile_config][0], h2 = kVariants[tile_config][1];
   if (tile_config == 0) {
