@@ -358,7 +358,8 @@ def main():
                      "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                      "frac_of_datasheet_2250": achieved / 2250.0,
                      "traffic": profile_traffic("prefill_dram_traffic.md") if S == SEQ else None,
-                     "traffic_note": "8k capture scaled x4 (profiles/prefill_dram_traffic.md)",
+                     "traffic_note": "one-pass ncu capture of the 32k launch "
+                                     "(profiles/prefill_dram_traffic.md)",
                      "kernel": "rel_attn_prefill_kernel (1 launch per step)",
                      "tile_config": args.tile_config},
         "gpu_launches": args.steps,
