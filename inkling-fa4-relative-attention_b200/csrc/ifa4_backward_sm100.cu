@@ -178,15 +178,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* vec = reinterpret_cast<float*>(smem + kSmemVec);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kvh = blockIdx.x;
-  const int b = blockIdx.y;
+  // Grid (key slots, kv heads, sequences) when the Q / dO stream over all heads outgrows L2
+  // (the key blocks of one kv head then run together and share their Q / dO tiles in L2),
+  // otherwise (kv heads, sequences, key slots).
+  const int kvh = a.slots_first_dkdv ? blockIdx.y : blockIdx.x;
+  const int b = a.slots_first_dkdv ? blockIdx.z : blockIdx.y;
+  const int kb0 = a.slots_first_dkdv ? blockIdx.x : blockIdx.z;
+  const int kb_step = a.slots_first_dkdv ? gridDim.x : gridDim.z;
   const int group = a.n_heads / a.kv_heads;
   const int q_start = a.cu_q[b];
   const int sq = a.cu_q[b + 1] - q_start;
   const int k_start = a.cu_k[b];
   const int sk = a.cu_k[b + 1] - k_start;
   const int n_kb = (sk + kBN - 1) / kBN;
-  if (static_cast<int>(blockIdx.z) >= n_kb) return;  // uniform over the CTA
+  if (kb0 >= n_kb) return;  // uniform over the CTA
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_kv = l2_policy_evict_first();
       const uint64_t pol_q = l2_policy_evict_last();
       bool ok = true;
-      for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
+      for (int kb = kb0; kb < n_kb && ok; kb += kb_step) {
         const KeyBlock blk = key_block(a, kb * kBN, sq, sk);
         if (blk.n_q == 0) continue;
         if (!(ok = mbar_wait(&bars->kv_empty, (ic & 1) ^ 1, ab))) break;
@@ -274,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_addr = smem_u32(smem + kSmemQ);
       const uint32_t do_addr = smem_u32(smem + kSmemDO);
       bool ok = true;
-      for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
+      for (int kb = kb0; kb < n_kb && ok; kb += kb_step) {
         const KeyBlock blk = key_block(a, kb * kBN, sq, sk);
         if (blk.n_q == 0) continue;
         if (!(ok = mbar_wait(&bars->kv_full, ic & 1, ab))) break;
@@ -353,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t sc = 0, ec = 0;
     bool ok = true;
-    for (int kb = blockIdx.z; kb < n_kb && ok; kb += gridDim.z) {
+    for (int kb = kb0; kb < n_kb && ok; kb += kb_step) {
       const int k0 = kb * kBN;
       const KeyBlock blk = key_block(a, k0, sq, sk);
       const int kl = k0 + r;  // this thread's key (local to the sequence)
@@ -615,15 +620,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + kSmemBar);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = blockIdx.x;
-  const int b = blockIdx.y;
+  // Grid (query slots, heads, sequences) when the K / V stream over all kv heads outgrows L2,
+  // otherwise (heads, sequences, query slots); as in the forward.
+  const int h = a.slots_first_dq ? blockIdx.y : blockIdx.x;
+  const int b = a.slots_first_dq ? blockIdx.z : blockIdx.y;
+  const int slot0 = a.slots_first_dq ? blockIdx.x : blockIdx.z;
+  const int slot_step = a.slots_first_dq ? gridDim.x : gridDim.z;
   const int kvh = h / (a.n_heads / a.kv_heads);
   const int q_start = a.cu_q[b];
   const int sq = a.cu_q[b + 1] - q_start;
   const int k_start = a.cu_k[b];
   const int sk = a.cu_k[b + 1] - k_start;
   const int n_qt = (sq + kBM - 1) / kBM;
-  if (static_cast<int>(blockIdx.z) >= n_qt) return;
+  if (slot0 >= n_qt) return;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->qdo_full, 1);
@@ -666,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_kv = l2_policy_evict_last();
       const uint64_t pol_q = l2_policy_evict_first();
       bool ok = true;
-      for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+      for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
         const int q0 = (n_qt - 1 - slot) * kBM;
         const QTile t = q_tile(a, q0, sq, sk);
         if (t.n_kv == 0) continue;
@@ -717,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t k_addr = smem_u32(smem + kSmemK);
       const uint32_t v_addr = smem_u32(smem + kSmemV);
       bool ok = true;
-      for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+      for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
         const int q0 = (n_qt - 1 - slot) * kBM;
         const QTile t = q_tile(a, q0, sq, sk);
         if (t.n_kv == 0) continue;
@@ -776,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint16_t* bias_buf = reinterpret_cast<uint16_t*>(smem + kSmemBias + (warp - 2) * kBiasWarpBytes);
     uint32_t sc = 0, ec = 0;
     bool ok = true;
-    for (int slot = blockIdx.z; slot < n_qt && ok; slot += gridDim.z) {
+    for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
       const int q0 = (n_qt - 1 - slot) * kBM;
       const QTile t = q_tile(a, q0, sq, sk);
       const int qi = q0 + r;
@@ -955,12 +964,14 @@ cudaError_t launch_backward_sm100(const BackwardKernelArgs& args, const CUtensor
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  dim3 kgrid(args.kv_heads, args.batch, k_slots);
+  const dim3 kgrid = args.slots_first_dkdv ? dim3(k_slots, args.kv_heads, args.batch)
+                                           : dim3(args.kv_heads, args.batch, k_slots);
   bwd::rel_attn_bwd_dkdv_kernel<<<kgrid, bwd::kThreads, bwd::kv::kSmemAlloc, stream>>>(
       args, tm_q, tm_k, tm_v, tm_do);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dim3 qgrid(args.n_heads, args.batch, q_slots);
+  const dim3 qgrid = args.slots_first_dq ? dim3(q_slots, args.n_heads, args.batch)
+                                         : dim3(args.n_heads, args.batch, q_slots);
   bwd::rel_attn_bwd_dq_kernel<<<qgrid, bwd::kThreads, bwd::q::kSmemAlloc, stream>>>(
       args, tm_q, tm_k, tm_v, tm_do);
   return cudaGetLastError();

@@ -615,6 +615,7 @@ int validate_backward(const IFA4BackwardParams* p) {
   if (p->drel_stride_t <= 0 || p->drel_stride_h <= 0)
     return fail(IFA4_ERR_INVALID_ARGUMENT, "backward: drel strides must be positive");
   if (p->batch > 65535) return fail(IFA4_ERR_UNSUPPORTED, "backward: batch > 65535");
+  if (p->n_heads > 65535) return fail(IFA4_ERR_UNSUPPORTED, "backward: n_heads > 65535");
   return IFA4_OK;
 }
 
@@ -689,6 +690,19 @@ int ifa4_backward_launch(const IFA4BackwardParams* p, void* workspace, size_t wo
   a.scale_log2 = p->softmax_scale * 1.4426950408889634f;
   a.bias_vec = aligned16(p->rel) && p->rel_stride_t % 8 == 0 && p->rel_stride_h % 8 == 0 &&
                p->rel_extent % 8 == 0;
+  // Grid orders (as in the forward): the slots of one head run together when the operand
+  // stream of a tile over all heads (512 bytes per token and head: Q and dO for dK/dV, K and V
+  // for dQ; average sequence, capped by the window) is more than a third of the L2.
+  {
+    int64_t span_q = (p->total_q + p->batch - 1) / p->batch;
+    int64_t span_k = (p->total_k + p->batch - 1) / p->batch;
+    if (p->window_left >= 0) {
+      if (p->window_left + 256 < span_q) span_q = p->window_left + 256;
+      if (p->window_left + 256 < span_k) span_k = p->window_left + 256;
+    }
+    a.slots_first_dkdv = span_q * p->n_heads * 512 > (48LL << 20);
+    a.slots_first_dq = span_k * p->kv_heads * 512 > (48LL << 20);
+  }
   a.status = status;
 
   CUtensorMap tq, tk, tv, tdo;

@@ -117,6 +117,10 @@ struct BackwardKernelArgs {
   float scale;               // softmax_scale
   float scale_log2;          // softmax_scale * log2(e)
   int bias_vec;              // rel 16-byte aligned and rel_extent % 8 == 0 (vector bias windows)
+  int slots_first_dkdv;      // dK/dV grid (key slots, kv heads, sequences) instead of
+                             // (kv heads, sequences, key slots)
+  int slots_first_dq;        // dQ grid (query slots, heads, sequences) instead of
+                             // (heads, sequences, query slots)
   int* status;
 };
 
