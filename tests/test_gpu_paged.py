@@ -6,7 +6,8 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_close, device_status_ok, np32, oracle_full, run_decode, run_prefill, to_dev
+from gpu_util import (assert_close, device_status_ok, np32, oracle_full, oracle_rows, run_decode,
+                      run_prefill, to_dev)
 from inkling_fa4 import inkling_fa4_rel_attention_decode_triton as decode_api
 from inkling_fa4 import inkling_fa4_rel_attention_triton as prefill_api
 from inkling_fa4.workloads import Case, make_case, page_kv
@@ -61,6 +62,25 @@ def test_paged_chunked_prefill_vs_oracle(page_size, window):
     got = paged_prefill(pc, **kw)
     assert torch.equal(got, run_prefill(c, **kw))
     assert_close(np32(got), oracle_full(c, 1 / 128, window_left=window, causal_align="bottom_right"))
+
+
+def test_long_chunked_prefill_query_slots_first():
+    """Chunks over ~14k-key caches with 8 KV heads: the key range of a query tile over all KV
+    heads (59 MB) exceeds a third of L2, so both the contiguous and the paged launch use the
+    (query slots, head slots, sequences) grid.  Paged equals contiguous bit for bit, and sampled
+    rows match the oracle."""
+    cache = [16000, 12500]
+    new = [300, 64]
+    total = [a + b for a, b in zip(cache, new)]
+    c = to_dev(make_case(new, total, 32, 8, 128, seed=21))
+    pc = page_kv(c, page_size=16, seed=21)
+    kw = dict(causal_align="bottom_right")
+    want = run_prefill(c, **kw)
+    got = paged_prefill(pc, **kw)
+    assert torch.equal(got, want), float((got.float() - want.float()).abs().max())
+    heads = [0, 13, 31]
+    toks, ref = oracle_rows(c, 12, heads, 1 / 128, causal_align="bottom_right", seed=4)
+    assert_close(np32(want[torch.from_numpy(toks).cuda()][:, heads]), ref)
 
 
 @pytest.mark.parametrize("page_size", [16, 32, 64, 128])
