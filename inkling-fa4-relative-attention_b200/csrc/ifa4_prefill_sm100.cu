@@ -513,33 +513,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         // raw scores and the scale is folded into the exponent FMA (mul = scale*log2e).
         // Otherwise every lane turns its scores into the scaled, biased, masked logit chunk by
         // chunk and writes it back over S in TMEM, and pass 2 reads logits (mul = 1).
+        // Score chunk 0 (columns 0..31) is pass 2's first operand: in interior warps pass 1
+        // leaves it in rr[0], so pass 2 starts without a TMEM round trip.
+        uint32_t rr[2][32];
         float mul, m_tile;
         if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
-          uint32_t r[4][32];
+          uint32_t r[3][32];  // score chunks 1..3
+          tmem_ld32(t_s, rr[0]);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
+          for (int c = 0; c < 3; ++c) tmem_ld32(t_s + (c + 1) * 32, r[c]);
           tmem_wait_ld();
-          // columns 0..3 start four chains; 4..123 in steps of 8 (a step at column 28 of a
-          // 32-column array continues into the next array); then 124..127
-          float mA = __uint_as_float(r[0][0]), mB = __uint_as_float(r[0][1]);
-          float mC = __uint_as_float(r[0][2]), mD = __uint_as_float(r[0][3]);
+          auto col = [&](int c) -> float {
+            return __uint_as_float(c < 32 ? rr[0][c] : r[(c >> 5) - 1][c & 31]);
+          };
+          // columns 0..3 start four chains, then 4..123 in steps of 8, then 124..127
+          float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
 #pragma unroll
           for (int c = 4; c < 124; c += 8) {
-            const int cc = c >> 5, i = c & 31;
-            if (i + 7 < 32) {
-              mA = fmax3(mA, __uint_as_float(r[cc][i]), __uint_as_float(r[cc][i + 1]));
-              mB = fmax3(mB, __uint_as_float(r[cc][i + 2]), __uint_as_float(r[cc][i + 3]));
-              mC = fmax3(mC, __uint_as_float(r[cc][i + 4]), __uint_as_float(r[cc][i + 5]));
-              mD = fmax3(mD, __uint_as_float(r[cc][i + 6]), __uint_as_float(r[cc][i + 7]));
-            } else {
-              mA = fmax3(mA, __uint_as_float(r[cc][28]), __uint_as_float(r[cc][29]));
-              mB = fmax3(mB, __uint_as_float(r[cc][30]), __uint_as_float(r[cc][31]));
-              mC = fmax3(mC, __uint_as_float(r[cc + 1][0]), __uint_as_float(r[cc + 1][1]));
-              mD = fmax3(mD, __uint_as_float(r[cc + 1][2]), __uint_as_float(r[cc + 1][3]));
-            }
+            mA = fmax3(mA, col(c), col(c + 1));
+            mB = fmax3(mB, col(c + 2), col(c + 3));
+            mC = fmax3(mC, col(c + 4), col(c + 5));
+            mD = fmax3(mD, col(c + 6), col(c + 7));
           }
-          mA = fmax3(mA, __uint_as_float(r[3][28]), __uint_as_float(r[3][29]));
-          mB = fmax3(mB, __uint_as_float(r[3][30]), __uint_as_float(r[3][31]));
+          mA = fmax3(mA, col(124), col(125));
+          mB = fmax3(mB, col(126), col(127));
           mul = a.scale_log2;
           m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
         } else {
@@ -608,6 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(t_s + c * 32, r);
           }
           tmem_wait_st();  // pass 2 reads these columns back
+          tmem_ld32(t_s, rr[0]);
+          tmem_wait_ld();
           mul = 1.f;
           m_tile = mx;
         }
@@ -624,16 +623,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
         __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
-        // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks, loading chunk c+1 while
-        // chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
+        // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks (chunk 0 already in rr[0]),
+        // loading chunk c+1 while chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
         // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
         // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
         const uint64_t mul2 = f2_pack(mul, mul);
         const uint64_t neg2 = f2_pack(-m_use, -m_use);
         uint64_t acc[4] = {0, 0, 0, 0};
-        uint32_t rr[2][32];
-        tmem_ld32(t_s, rr[0]);
-        tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
