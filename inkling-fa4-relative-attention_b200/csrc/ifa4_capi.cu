@@ -281,8 +281,7 @@ const char* ifa4_prefill_tile_config_name(int32_t tile_config) {
       "sm100_q2x128_kv128_d128_ws12_emu2of16", "sm100_q2x128_kv128_d128_ws12_emu4of16",
       "sm100_q2x128_kv128_d128_ws12_emu6of16", "sm100_q2x128_kv128_d128_ws12_emu8of16",
       "sm100_q2x128_kv128_d128_ws12_h2x16of16", "sm100_q2x128_kv128_d128_ws12_h2x8of16",
-      "sm100_q2x128_kv128_d128_ws12_emu4h2x8of16", "sm100_q2x128_kv2x64_d128_ws12_emu0of16",
-      "sm100_q2x128_kv2x64_d128_ws12_emu4of16"};
+      "sm100_q2x128_kv128_d128_ws12_emu4h2x8of16"};
   if (tile_config < 0 || tile_config >= ifa4::kPrefillNumTileConfigs) return "";
   return names[tile_config];
 }
@@ -294,7 +293,7 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   if (ifa4::prefill_emulated_exp_columns(p->tile_config) < 0)
     return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d unknown", p->tile_config);
   if (p->block_table != nullptr && !ifa4::prefill_paged_tile_config_ok(p->tile_config))
-    return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d has no paged-cache variant (0, 1, 3, 9, 10)",
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d has no paged-cache variant (0, 1, 3)",
                 p->tile_config);
   if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
   int* status = nullptr;

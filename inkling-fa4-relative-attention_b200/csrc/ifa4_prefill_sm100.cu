@@ -70,8 +70,6 @@ constexpr float kRescaleThreshold = 8.0f;                // log2 units: rescale 
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, /*b_mn_major=*/true);
 
-constexpr uint32_t kIdescQKHalf = idesc_bf16_f32(128, 64, /*b_mn_major=*/false);
-
 struct Bars {
   uint64_t q_full, q_empty;
   uint64_t k_full[2], k_empty[2];
@@ -79,10 +77,6 @@ struct Bars {
   uint64_t s_full[2], p_full[2];
   uint64_t o_full[2], o_empty[2];
   uint64_t drain;
-  // split-score kernels (kSplit): per sub-tile s and key half h, S_s^h ready / P_s^h ready;
-  // pv_done[s] completes once per P.V half issued for sub-tile s
-  uint64_t s_half[2][2], p_half[2][2];
-  uint64_t pv_done[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -265,32 +259,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint3
   }
 }
 
-// Split-score variants: S_s = Q_s K^T is computed as two 64-key halves (N = 64), S_s^h in TMEM
-// columns [64 h, 64 h + 64) of the sub-tile's S region; P_s^h is written over the first 32 of
-// them and O_s += P_s^h V[64 h, 64 h + 64) reads it from there.
-__device__ __forceinline__ void issue_qk_half(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr,
-                                              int h) {
-  const uint64_t qd = sdesc_sw128(q_addr, 16, 1024);
-  const uint64_t kd = sdesc_sw128(k_addr + h * 8192, 16, 1024);  // key rows 64 h.. (8 atoms)
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-    umma_ss(tmem_s, sdesc_advance(qd, off), sdesc_advance(kd, off), kIdescQKHalf,
-            kk > 0 ? 1u : 0u);
-  }
-}
-
-__device__ __forceinline__ void issue_pv_half(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_addr,
-                                              int h, bool accumulate) {
-  const uint64_t vd = sdesc_sw128(v_addr, kHalf, 1024);
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    umma_ts(tmem_o, tmem_p + kk * 8, sdesc_advance(vd, (h * 4 + kk) * 2048), kIdescPV,
-            (kk > 0 || accumulate) ? 1u : 0u);
-  }
-}
-
-template <int kEmu, int kHalf2, bool kPaged, bool kSplit>
+template <int kEmu, int kHalf2, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
                             const __grid_constant__ CUtensorMap tm_q,
@@ -334,13 +303,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->o_empty[i], 4);
     }
     mbar_init(&bars->drain, 1);
-    for (int i = 0; i < 2; ++i) {
-      for (int h = 0; h < 2; ++h) {
-        mbar_init(&bars->s_half[i][h], 1);
-        mbar_init(&bars->p_half[i][h], 4);
-      }
-      mbar_init(&bars->pv_done[i], 1);
-    }
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -414,74 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
    } else if (warp == 1) {
     // ------------------------------------------------------------------ UMMA issuer
-    if (kSplit && lane == 0) {
-      // Per KV tile j and (sub-tile s, key half h), in this order: wait P_s^h(j-1), then
-      // O_s += P_s^h(j-1) V(j-1)[half h] (commit pv_done[s]) and S_s^h(j) = Q_s K(j)[half h]^T
-      // (commit s_half[s][h]).  Only S_s^h's own half waits for its P.V, so the other half's
-      // score MMA is never behind the softmax of this one.
-      uint32_t qc = 0, kc = 0, vc = 0, pc = 0, oc = 0;
-      const uint32_t q_addr = smem_u32(smem + kSmemQ);
-      const uint32_t k_addr = smem_u32(smem + kSmemK);
-      const uint32_t v_addr = smem_u32(smem + kSmemV);
-      bool ok = true;
-      for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
-        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
-        if (t.n_kv == 0) continue;
-        if (!(ok = mbar_wait(&bars->q_full, qc & 1, ab))) break;
-        ++qc;
-        uint32_t ks = kc & 1;
-        if (!(ok = mbar_wait(&bars->k_full[ks], (kc >> 1) & 1, ab))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            issue_qk_half(tbase + s * 128 + h * 64, q_addr + s * kTile, k_addr + ks * kTile, h);
-            umma_commit(&bars->s_half[s][h]);
-          }
-        umma_commit(&bars->k_empty[ks]);
-        ++kc;
-        for (int j = 1; j <= t.n_kv && ok; ++j) {
-          const bool last = j == t.n_kv;  // only the P.V of tile j - 1 remains
-          ks = kc & 1;
-          const uint32_t vs = vc & 1;
-          if (!last && !(ok = mbar_wait(&bars->k_full[ks], (kc >> 1) & 1, ab))) break;
-#pragma unroll
-          for (int s = 0; s < 2 && ok; ++s)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (!(ok = mbar_wait(&bars->p_half[s][h], pc & 1, ab))) break;
-              if (j == 1 && h == 0 && !(ok = mbar_wait(&bars->o_empty[s], (oc & 1) ^ 1, ab))) break;
-              if (s == 0 && h == 0 && !(ok = mbar_wait(&bars->v_full[vs], (vc >> 1) & 1, ab)))
-                break;
-              tc_fence_after();
-              issue_pv_half(tbase + 256 + s * 128, tbase + s * 128 + h * 64, v_addr + vs * kTile,
-                            h, j > 1 || h > 0);
-              umma_commit(&bars->pv_done[s]);
-              if (last) {
-                if (h == 1) umma_commit(&bars->o_full[s]);
-              } else {
-                issue_qk_half(tbase + s * 128 + h * 64, q_addr + s * kTile, k_addr + ks * kTile,
-                              h);
-                umma_commit(&bars->s_half[s][h]);
-              }
-            }
-          if (!ok) break;
-          ++pc;
-          if (!last) {
-            umma_commit(&bars->k_empty[ks]);
-            ++kc;
-          }
-          umma_commit(&bars->v_empty[vs]);
-          ++vc;
-        }
-        if (!ok) break;
-        umma_commit(&bars->q_empty);
-        ++oc;
-      }
-      umma_commit(&bars->drain);
-      mbar_wait(&bars->drain, 0, ab);
-    } else if (lane == 0) {
+    if (lane == 0) {
       uint32_t qc = 0, kc = 0, vc = 0, pc = 0, oc = 0;
       const uint32_t q_addr = smem_u32(smem + kSmemQ);
       const uint32_t k_addr = smem_u32(smem + kSmemK);
@@ -558,7 +453,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ms = a.align_bottom_right ? sk - sq : 0;
     const int bs = a.align_bottom_right ? sk - sq : sq - sk;
     uint32_t pc = 0, oc = 0;
-    uint32_t st = 0;  // split-score kernels: P halves released so far
     bool ok = true;
     for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
       const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
@@ -594,369 +488,199 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint16_t* bias_buf = reinterpret_cast<uint16_t*>(smem + kSmemBias + (warp - 4) * kBiasWarpBytes);
       float m_run = -INFINITY, l_run = 0.f;
 
-      if constexpr (kSplit) {
-        // Two 64-key halves per KV tile; everything of a half stays in registers (S is read
-        // from TMEM once, logits of bias/mask halves are never written back).
-        for (int j = 0; j < t.n_kv && ok; ++j) {
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            const int kb = (t.j_lo + j) * kBN + hh * 64;  // key at column 0 of this half
-            const int bl = dmax - a.rel_extent + 1 - kb;  // first column with bias
-            const int bh = dmax - kb;                     // last column with bias
-            const int cl = key_lo - kb, ch = key_hi - kb;  // visible columns [cl, ch)
-            const bool has_bias = row_valid && bl <= 63 && bh >= 0;
-            const bool has_mask = cl > 0 || ch < 64;
-            const bool warp_bias = __any_sync(0xffffffffu, has_bias);
-            uint32_t bwin[2][20];
-            if (a.bias_vec && warp_bias) {
+      for (int j = 0; j < t.n_kv; ++j) {
+        const int k0 = (t.j_lo + j) * kBN;
+        // relative bias: keys in [dmax - R + 1, dmax] carry rel[row, dmax - key]
+        const int bl = dmax - a.rel_extent + 1 - k0;  // first column with bias
+        const int bh = dmax - k0;                     // last column with bias
+        const int cl = key_lo - k0, ch = key_hi - k0;  // visible columns [cl, ch)
+        const bool has_bias = row_valid && bl <= 127 && bh >= 0;
+        const bool has_mask = cl > 0 || ch < kBN;
+        const bool warp_bias = __any_sync(0xffffffffu, has_bias);
+        // Vector bias path: the first two chunks' windows are loaded before S arrives, so their
+        // round trip overlaps the wait; chunk c + 2 is loaded when chunk c has been used.
+        uint32_t bwin[2][20];
+        if (a.bias_vec && warp_bias) {
 #pragma unroll
-              for (int cc = 0; cc < 2; ++cc)
-                load_bias_window(rel_row, bh, cc, a.rel_extent,
-                                 has_bias && cc * 32 + 31 >= bl && cc * 32 <= bh, bwin[cc]);
-            }
-            if (!(ok = mbar_wait_warp(&bars->s_half[s][hh], pc & 1, ab))) break;
-            tc_fence_after();
-            uint32_t r[2][32];
-            tmem_ld32(t_s + hh * 64, r[0]);
-            tmem_ld32(t_s + hh * 64 + 32, r[1]);
-            tmem_wait_ld();
-            float mul, m_tile;
-            if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
-              auto col = [&](int c) -> float { return __uint_as_float(r[c >> 5][c & 31]); };
-              float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
-#pragma unroll
-              for (int c = 4; c < 60; c += 8) {
-                mA = fmax3(mA, col(c), col(c + 1));
-                mB = fmax3(mB, col(c + 2), col(c + 3));
-                mC = fmax3(mC, col(c + 4), col(c + 5));
-                mD = fmax3(mD, col(c + 6), col(c + 7));
-              }
-              mA = fmax3(mA, col(60), col(61));
-              mB = fmax3(mB, col(62), col(63));
-              mul = a.scale_log2;
-              m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
-            } else {
-              float mx = -INFINITY;
-#pragma unroll
-              for (int c = 0; c < 2; ++c) {
-                float x[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[c][i]) * a.scale_log2;
-                const bool chunk_bias = has_bias && c * 32 + 31 >= bl && c * 32 <= bh;
-                if (a.bias_vec) {
-                  if (__any_sync(0xffffffffu, chunk_bias)) add_bias_window(bwin[c], bh, c, x);
-                } else if (__any_sync(0xffffffffu, chunk_bias)) {
-                  // cooperative gather through the warp's transpose buffer (as in the
-                  // whole-tile path)
-                  const int colw = c * 32 + lane;
-                  uint16_t v[32];
-#pragma unroll
-                  for (int tr = 0; tr < 32; ++tr) {
-                    const int qi_t = qi - lane + tr;
-                    const int d = qi_t + bs - kb - colw;
-                    v[tr] = 0;
-                    if (qi_t < sq && d >= 0 && d < a.rel_extent)
-                      v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
-                  }
-#pragma unroll
-                  for (int tr = 0; tr < 32; ++tr) bias_buf[tr * kBiasRowHalves + lane] = v[tr];
-                  __syncwarp();
-                  const uint32_t* w =
-                      reinterpret_cast<const uint32_t*>(bias_buf) + lane * (kBiasRowHalves / 2);
-#pragma unroll
-                  for (int k = 0; k < 16; ++k) {
-                    const uint32_t pr = w[k];
-                    x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
-                    x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
-                  }
-                  __syncwarp();
-                }
-                if (has_mask) {
-#pragma unroll
-                  for (int i = 0; i < 32; ++i) {
-                    const int cc = c * 32 + i;
-                    if (cc < cl || cc >= ch) x[i] = -INFINITY;
-                  }
-                }
-                float m0 = x[0], m1 = x[1];
-#pragma unroll
-                for (int i = 2; i < 30; i += 4) {
-                  m0 = fmax3(m0, x[i], x[i + 1]);
-                  m1 = fmax3(m1, x[i + 2], x[i + 3]);
-                }
-                m0 = fmax3(m0, x[30], x[31]);
-                mx = fmax3(mx, m0, m1);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) r[c][i] = __float_as_uint(x[i]);
-              }
-              mul = 1.f;
-              m_tile = mx;
-            }
-            const float m_new = fmaxf(m_run, m_tile);
-            float alpha = 1.f;
-            bool need_rescale = false;
-            if (m_run == -INFINITY) {  // nothing accumulated yet: O and l hold (almost) 0
-              m_run = m_new;
-            } else if (m_new > m_run + kRescaleThreshold) {
-              alpha = fast_exp2(m_run - m_new);
-              need_rescale = true;
-              l_run *= alpha;
-              m_run = m_new;
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-            __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
-            const uint64_t mul2 = f2_pack(mul, mul);
-            const uint64_t neg2 = f2_pack(-m_use, -m_use);
-            uint64_t acc[4] = {0, 0, 0, 0};
-            uint32_t pk[32];
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int cc = c * 32 + 2 * i;
-                float y0, y1;
-                f2_unpack(f2_fma(f2_pack(__uint_as_float(r[c][2 * i]),
-                                         __uint_as_float(r[c][2 * i + 1])),
-                                 mul2, neg2),
-                          y0, y1);
-                float p0, p1;
-                if ((cc & 15) < kEmu) {
-                  exp2_poly_pair(y0, y1, p0, p1);
-                } else if ((cc & 15) < kEmu + kHalf2) {
-                  exp2_h2_pair(y0, y1, p0, p1);
-                } else {
-                  p0 = fast_exp2(y0);
-                  p1 = fast_exp2(y1);
-                }
-                acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
-                pk[c * 16 + i] = pack_bf16x2(p0, p1);
-              }
-            }
-            tmem_st32(t_s + hh * 64, pk);
-            {
-              const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
-              float u0, u1;
-              f2_unpack(f2_add(a01, a23), u0, u1);
-              l_run += u0 + u1;
-            }
-            if (__any_sync(0xffffffffu, need_rescale)) {
-              // O_s may still be receiving the P.V of the previous half (every earlier one
-              // completed before this half's S was committed): wait for it, then rescale.
-              if (!(ok = mbar_wait_warp(&bars->pv_done[s], (st - 1) & 1, ab))) break;
-              tc_fence_after();
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                uint32_t o[32];
-                tmem_ld32(t_o + c * 32, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                tmem_st32(t_o + c * 32, o);
-              }
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_half[s][hh]);
-            ++st;
-          }
-          ++pc;
+          for (int cc = 0; cc < 2; ++cc)
+            load_bias_window(rel_row, bh, cc, a.rel_extent,
+                             has_bias && cc * 32 + 31 >= bl && cc * 32 <= bh, bwin[cc]);
         }
-      } else {
-        for (int j = 0; j < t.n_kv; ++j) {
-          const int k0 = (t.j_lo + j) * kBN;
-          // relative bias: keys in [dmax - R + 1, dmax] carry rel[row, dmax - key]
-          const int bl = dmax - a.rel_extent + 1 - k0;  // first column with bias
-          const int bh = dmax - k0;                     // last column with bias
-          const int cl = key_lo - k0, ch = key_hi - k0;  // visible columns [cl, ch)
-          const bool has_bias = row_valid && bl <= 127 && bh >= 0;
-          const bool has_mask = cl > 0 || ch < kBN;
-          const bool warp_bias = __any_sync(0xffffffffu, has_bias);
-          // Vector bias path: the first two chunks' windows are loaded before S arrives, so their
-          // round trip overlaps the wait; chunk c + 2 is loaded when chunk c has been used.
-          uint32_t bwin[2][20];
-          if (a.bias_vec && warp_bias) {
-  #pragma unroll
-            for (int cc = 0; cc < 2; ++cc)
-              load_bias_window(rel_row, bh, cc, a.rel_extent,
-                               has_bias && cc * 32 + 31 >= bl && cc * 32 <= bh, bwin[cc]);
+        if (!(ok = mbar_wait_warp(&bars->s_full[s], pc & 1, ab))) break;
+        ++pc;
+        tc_fence_after();
+        // Pass 1 — the row max.  In a warp where no row needs bias or mask it is taken over the
+        // raw scores and the scale is folded into the exponent FMA (mul = scale*log2e).
+        // Otherwise every lane turns its scores into the scaled, biased, masked logit chunk by
+        // chunk and writes it back over S in TMEM, and pass 2 reads logits (mul = 1).
+        // Score chunk 0 (columns 0..31) is pass 2's first operand: in interior warps pass 1
+        // leaves it in rr[0], so pass 2 starts without a TMEM round trip.
+        uint32_t rr[2][32];
+        float mul, m_tile;
+        if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
+          uint32_t r[3][32];  // score chunks 1..3
+          tmem_ld32(t_s, rr[0]);
+#pragma unroll
+          for (int c = 0; c < 3; ++c) tmem_ld32(t_s + (c + 1) * 32, r[c]);
+          tmem_wait_ld();
+          auto col = [&](int c) -> float {
+            return __uint_as_float(c < 32 ? rr[0][c] : r[(c >> 5) - 1][c & 31]);
+          };
+          // columns 0..3 start four chains, then 4..123 in steps of 8, then 124..127
+          float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
+#pragma unroll
+          for (int c = 4; c < 124; c += 8) {
+            mA = fmax3(mA, col(c), col(c + 1));
+            mB = fmax3(mB, col(c + 2), col(c + 3));
+            mC = fmax3(mC, col(c + 4), col(c + 5));
+            mD = fmax3(mD, col(c + 6), col(c + 7));
           }
-          if (!(ok = mbar_wait_warp(&bars->s_full[s], pc & 1, ab))) break;
-          ++pc;
-          tc_fence_after();
-          // Pass 1 — the row max.  In a warp where no row needs bias or mask it is taken over the
-          // raw scores and the scale is folded into the exponent FMA (mul = scale*log2e).
-          // Otherwise every lane turns its scores into the scaled, biased, masked logit chunk by
-          // chunk and writes it back over S in TMEM, and pass 2 reads logits (mul = 1).
-          // Score chunk 0 (columns 0..31) is pass 2's first operand: in interior warps pass 1
-          // leaves it in rr[0], so pass 2 starts without a TMEM round trip.
-          uint32_t rr[2][32];
-          float mul, m_tile;
-          if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
-            uint32_t r[3][32];  // score chunks 1..3
-            tmem_ld32(t_s, rr[0]);
-  #pragma unroll
-            for (int c = 0; c < 3; ++c) tmem_ld32(t_s + (c + 1) * 32, r[c]);
-            tmem_wait_ld();
-            auto col = [&](int c) -> float {
-              return __uint_as_float(c < 32 ? rr[0][c] : r[(c >> 5) - 1][c & 31]);
-            };
-            // columns 0..3 start four chains, then 4..123 in steps of 8, then 124..127
-            float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
-  #pragma unroll
-            for (int c = 4; c < 124; c += 8) {
-              mA = fmax3(mA, col(c), col(c + 1));
-              mB = fmax3(mB, col(c + 2), col(c + 3));
-              mC = fmax3(mC, col(c + 4), col(c + 5));
-              mD = fmax3(mD, col(c + 6), col(c + 7));
-            }
-            mA = fmax3(mA, col(124), col(125));
-            mB = fmax3(mB, col(126), col(127));
-            mul = a.scale_log2;
-            m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
-          } else {
-            float mx = -INFINITY;
-  #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint32_t r[32];
-              tmem_ld32(t_s + c * 32, r);
-              tmem_wait_ld();
-              float x[32];
-  #pragma unroll
-              for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
-              // Relative bias, gathered by the whole warp: for each of the warp's 32 rows the
-              // lanes load that row's 32 consecutive values (one coalesced 64-byte access),
-              // store them to the transpose buffer, and each lane then reads its own row.
-              // Columns outside [bl, bh] (or rows without bias) read 0.
-              const bool chunk_bias = has_bias && c * 32 + 31 >= bl && c * 32 <= bh;
-              if (a.bias_vec) {
-                if (__any_sync(0xffffffffu, chunk_bias)) add_bias_window(bwin[c & 1], bh, c, x);
-                if (c < 2 && warp_bias)
-                  load_bias_window(rel_row, bh, c + 2, a.rel_extent,
-                                   has_bias && (c + 2) * 32 + 31 >= bl && (c + 2) * 32 <= bh,
-                                   bwin[c & 1]);
-              } else if (__any_sync(0xffffffffu, chunk_bias)) {
-                uint16_t* buf = bias_buf;
-                const int col = c * 32 + lane;
-                uint16_t v[32];
-  #pragma unroll
-                for (int tr = 0; tr < 32; ++tr) {  // all 32 loads in flight before any use
-                  const int qi_t = qi - lane + tr;  // row of lane tr in this warp
-                  const int d = qi_t + bs - k0 - col;
-                  v[tr] = 0;
-                  if (qi_t < sq && d >= 0 && d < a.rel_extent)
-                    v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
-                }
-  #pragma unroll
-                for (int tr = 0; tr < 32; ++tr) buf[tr * kBiasRowHalves + lane] = v[tr];
-                __syncwarp();
-                const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + lane * (kBiasRowHalves / 2);
-  #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                  const uint32_t pr = w[k];
-                  x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
-                  x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
-                }
-                __syncwarp();
-              }
-              if (has_mask) {
-  #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  const int col = c * 32 + i;
-                  if (col < cl || col >= ch) x[i] = -INFINITY;
-                }
-              }
-              float m0 = x[0], m1 = x[1];
-  #pragma unroll
-              for (int i = 2; i < 30; i += 4) {  // columns 2..29, then 30 and 31
-                m0 = fmax3(m0, x[i], x[i + 1]);
-                m1 = fmax3(m1, x[i + 2], x[i + 3]);
-              }
-              m0 = fmax3(m0, x[30], x[31]);
-              mx = fmax3(mx, m0, m1);
-  #pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
-              __syncwarp();  // reconverge after the per-row branches: tcgen05.st is .aligned
-              tmem_st32(t_s + c * 32, r);
-            }
-            tmem_wait_st();  // pass 2 reads these columns back
-            tmem_ld32(t_s, rr[0]);
-            tmem_wait_ld();
-            mul = 1.f;
-            m_tile = mx;
-          }
-          const float m_new = fmaxf(m_run, m_tile);
-          float alpha = 1.f;
-          bool need_rescale = false;
-          if (j == 0) {
-            m_run = m_new;
-          } else if (m_new > m_run + kRescaleThreshold) {
-            alpha = fast_exp2(m_run - m_new);
-            need_rescale = true;
-            l_run *= alpha;
-            m_run = m_new;
-          }
-          const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-          __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
-          // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks (chunk 0 already in rr[0]),
-          // loading chunk c+1 while chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
-          // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
-          // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
-          const uint64_t mul2 = f2_pack(mul, mul);
-          const uint64_t neg2 = f2_pack(-m_use, -m_use);
-          uint64_t acc[4] = {0, 0, 0, 0};
-  #pragma unroll
+          mA = fmax3(mA, col(124), col(125));
+          mB = fmax3(mB, col(126), col(127));
+          mul = a.scale_log2;
+          m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
+        } else {
+          float mx = -INFINITY;
+#pragma unroll
           for (int c = 0; c < 4; ++c) {
-            if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
-            uint32_t pk[16];
-  #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int col = c * 32 + 2 * i;
-              float y0, y1;
-              f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[c & 1][2 * i]),
-                                       __uint_as_float(rr[c & 1][2 * i + 1])),
-                               mul2, neg2),
-                        y0, y1);
-              float p0, p1;
-              if ((col & 15) < kEmu) {
-                exp2_poly_pair(y0, y1, p0, p1);
-              } else if ((col & 15) < kEmu + kHalf2) {
-                exp2_h2_pair(y0, y1, p0, p1);
-              } else {
-                p0 = fast_exp2(y0);
-                p1 = fast_exp2(y1);
+            uint32_t r[32];
+            tmem_ld32(t_s + c * 32, r);
+            tmem_wait_ld();
+            float x[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
+            // Relative bias, gathered by the whole warp: for each of the warp's 32 rows the
+            // lanes load that row's 32 consecutive values (one coalesced 64-byte access),
+            // store them to the transpose buffer, and each lane then reads its own row.
+            // Columns outside [bl, bh] (or rows without bias) read 0.
+            const bool chunk_bias = has_bias && c * 32 + 31 >= bl && c * 32 <= bh;
+            if (a.bias_vec) {
+              if (__any_sync(0xffffffffu, chunk_bias)) add_bias_window(bwin[c & 1], bh, c, x);
+              if (c < 2 && warp_bias)
+                load_bias_window(rel_row, bh, c + 2, a.rel_extent,
+                                 has_bias && (c + 2) * 32 + 31 >= bl && (c + 2) * 32 <= bh,
+                                 bwin[c & 1]);
+            } else if (__any_sync(0xffffffffu, chunk_bias)) {
+              uint16_t* buf = bias_buf;
+              const int col = c * 32 + lane;
+              uint16_t v[32];
+#pragma unroll
+              for (int tr = 0; tr < 32; ++tr) {  // all 32 loads in flight before any use
+                const int qi_t = qi - lane + tr;  // row of lane tr in this warp
+                const int d = qi_t + bs - k0 - col;
+                v[tr] = 0;
+                if (qi_t < sq && d >= 0 && d < a.rel_extent)
+                  v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
               }
-              acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
-              pk[i] = pack_bf16x2(p0, p1);
+#pragma unroll
+              for (int tr = 0; tr < 32; ++tr) buf[tr * kBiasRowHalves + lane] = v[tr];
+              __syncwarp();
+              const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + lane * (kBiasRowHalves / 2);
+#pragma unroll
+              for (int k = 0; k < 16; ++k) {
+                const uint32_t pr = w[k];
+                x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
+                x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
+              }
+              __syncwarp();
             }
-            tmem_st16(t_s + c * 16, pk);
-            if (c < 3) tmem_wait_ld();
-          }
-          {
-            const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
-            float u0, u1;
-            f2_unpack(f2_add(a01, a23), u0, u1);
-            l_run += u0 + u1;
-          }
-          // Conditional O correction (PV of the previous tile is complete: its commit
-          // preceded this tile's S commit).
-          if (__any_sync(0xffffffffu, need_rescale)) {
-  #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint32_t o[32];
-              tmem_ld32(t_o + c * 32, o);
-              tmem_wait_ld();
-  #pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(t_o + c * 32, o);
+            if (has_mask) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int col = c * 32 + i;
+                if (col < cl || col >= ch) x[i] = -INFINITY;
+              }
             }
+            float m0 = x[0], m1 = x[1];
+#pragma unroll
+            for (int i = 2; i < 30; i += 4) {  // columns 2..29, then 30 and 31
+              m0 = fmax3(m0, x[i], x[i + 1]);
+              m1 = fmax3(m1, x[i + 2], x[i + 3]);
+            }
+            m0 = fmax3(m0, x[30], x[31]);
+            mx = fmax3(mx, m0, m1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
+            __syncwarp();  // reconverge after the per-row branches: tcgen05.st is .aligned
+            tmem_st32(t_s + c * 32, r);
           }
-          // every lane's TMEM stores are complete and fenced before lane 0 releases P
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->p_full[s]);
+          tmem_wait_st();  // pass 2 reads these columns back
+          tmem_ld32(t_s, rr[0]);
+          tmem_wait_ld();
+          mul = 1.f;
+          m_tile = mx;
         }
+        const float m_new = fmaxf(m_run, m_tile);
+        float alpha = 1.f;
+        bool need_rescale = false;
+        if (j == 0) {
+          m_run = m_new;
+        } else if (m_new > m_run + kRescaleThreshold) {
+          alpha = fast_exp2(m_run - m_new);
+          need_rescale = true;
+          l_run *= alpha;
+          m_run = m_new;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
+        // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks (chunk 0 already in rr[0]),
+        // loading chunk c+1 while chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
+        // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
+        // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
+        const uint64_t mul2 = f2_pack(mul, mul);
+        const uint64_t neg2 = f2_pack(-m_use, -m_use);
+        uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            float y0, y1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[c & 1][2 * i]),
+                                     __uint_as_float(rr[c & 1][2 * i + 1])),
+                             mul2, neg2),
+                      y0, y1);
+            float p0, p1;
+            if ((col & 15) < kEmu) {
+              exp2_poly_pair(y0, y1, p0, p1);
+            } else if ((col & 15) < kEmu + kHalf2) {
+              exp2_h2_pair(y0, y1, p0, p1);
+            } else {
+              p0 = fast_exp2(y0);
+              p1 = fast_exp2(y1);
+            }
+            acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(t_s + c * 16, pk);
+          if (c < 3) tmem_wait_ld();
+        }
+        {
+          const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+          float u0, u1;
+          f2_unpack(f2_add(a01, a23), u0, u1);
+          l_run += u0 + u1;
+        }
+        // Conditional O correction (PV of the previous tile is complete: its commit
+        // preceded this tile's S commit).
+        if (__any_sync(0xffffffffu, need_rescale)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_o + c * 32, o);
+          }
+        }
+        // every lane's TMEM stores are complete and fenced before lane 0 releases P
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[s]);
       }
       if (!ok) break;
       // epilogue: O / l -> bf16, staged through this sub-tile's Q buffer (idle once O is final:
@@ -1031,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace prefill
 
 namespace {
-template <int kEmu, int kHalf2, bool kPaged, bool kSplit = false>
+template <int kEmu, int kHalf2, bool kPaged>
 cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
                            cudaStream_t stream) {
@@ -1042,27 +766,25 @@ cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kSplit>,
+    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(prefill::kSmemAlloc));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kSplit>
+  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>
       <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
   return cudaGetLastError();
 }
 }  // namespace
 
-// tile_config -> (columns of 16 on the FMA-pipe polynomial, columns of 16 on SFU f16x2,
-// split-score kernel)
-static const int kVariants[kPrefillNumTileConfigs][3] = {
-    {kPrefillDefaultEmu, kPrefillDefaultHalf2, 0}, {0, 0, 0}, {2, 0, 0}, {4, 0, 0}, {6, 0, 0},
-    {8, 0, 0}, {0, 16, 0}, {0, 8, 0}, {4, 8, 0}, {0, 0, 1}, {4, 0, 1}};
+// tile_config -> (columns of 16 on the FMA-pipe polynomial, columns of 16 on SFU f16x2)
+static const int kVariants[kPrefillNumTileConfigs][2] = {
+    {kPrefillDefaultEmu, kPrefillDefaultHalf2}, {0, 0}, {2, 0}, {4, 0}, {6, 0}, {8, 0},
+    {0, 16}, {0, 8}, {4, 8}};
 
 bool prefill_paged_tile_config_ok(int tile_config) {
-  return tile_config == 0 || tile_config == 1 || tile_config == 3 || tile_config == 9 ||
-         tile_config == 10;
+  return tile_config == 0 || tile_config == 1 || tile_config == 3;
 }
 
 int prefill_emulated_exp_columns(int tile_config) {
@@ -1079,7 +801,6 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
                              : dim3(head_slots, args.batch, q_slots);
   if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return cudaErrorInvalidValue;
   int emu = kVariants[tile_config][0], h2 = kVariants[tile_config][1];
-  const bool split = kVariants[tile_config][2] != 0;
   if (tile_config == 0) {
     // Measured on B200 (interleaved A/B, GQA 32/8): on long causal sequences the SFU is the
     // softmax bottleneck and 4 of 16 exponentials on the FMA pipe win (32k: 975 vs 921
@@ -1088,19 +809,9 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
     emu = (args.window_left < 0 && max_seqlen_q >= 16384) ? 4 : 0;
     h2 = 0;
   }
-  if (args.block_table != nullptr) {  // paged cache: the variants the automatic choice uses
-    if (split) {
-      if (emu == 0) return launch_variant<0, 0, true, true>(args, tm_q, tm_k, tm_v, grid, stream);
-      if (emu == 4) return launch_variant<4, 0, true, true>(args, tm_q, tm_k, tm_v, grid, stream);
-      return cudaErrorInvalidValue;
-    }
+  if (args.block_table != nullptr) {  // paged cache: the two variants the automatic choice uses
     if (emu == 0 && h2 == 0) return launch_variant<0, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
     if (emu == 4 && h2 == 0) return launch_variant<4, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
-    return cudaErrorInvalidValue;
-  }
-  if (split) {
-    if (emu == 0) return launch_variant<0, 0, false, true>(args, tm_q, tm_k, tm_v, grid, stream);
-    if (emu == 4) return launch_variant<4, 0, false, true>(args, tm_q, tm_k, tm_v, grid, stream);
     return cudaErrorInvalidValue;
   }
 #define IFA4_VARIANT(E, H) \

@@ -38,8 +38,6 @@ TILE_CONFIGS = {
     6: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 16},
     7: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 8},
     8: {"emulated_exp_of_16": 4, "sfu_f16x2_of_16": 8},
-    9: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 0, "score_halves": 2},
-    10: {"emulated_exp_of_16": 4, "sfu_f16x2_of_16": 0, "score_halves": 2},
 }
 # Interleaved A/B on one B200 (7 rounds x 5 calls, medians), 32k GQA 32/8, TFLOP/s:
 #   causal:      tc1 920.8  tc3 974.7  tc6 873.3  tc7 934.8  tc8 936.0
