@@ -509,171 +509,224 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait_warp(&bars->s_full[s], pc & 1, ab))) break;
         ++pc;
         tc_fence_after();
-        // Pass 1 — the row max.  In a warp where no row needs bias or mask it is taken over the
-        // raw scores and the scale is folded into the exponent FMA (mul = scale*log2e).
-        // Otherwise every lane turns its scores into the scaled, biased, masked logit chunk by
-        // chunk and writes it back over S in TMEM, and pass 2 reads logits (mul = 1).
-        // Score chunk 0 (columns 0..31) is pass 2's first operand: in interior warps pass 1
-        // leaves it in rr[0], so pass 2 starts without a TMEM round trip.
-        uint32_t rr[2][32];
-        float mul, m_tile;
-        if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
-          uint32_t r[3][32];  // score chunks 1..3
-          tmem_ld32(t_s, rr[0]);
-#pragma unroll
-          for (int c = 0; c < 3; ++c) tmem_ld32(t_s + (c + 1) * 32, r[c]);
+        // Interior tiles after the first: the exponentials are taken against the running max
+        // m_run without a row-max pass.  A score above m_run only makes its p larger than 1,
+        // which fp32 sums and bf16 P hold exactly as well up to 2^32; the tile's sum of p shows
+        // whether any went past that (or overflowed).  P stays in registers until then, so if
+        // one did, S is still intact in TMEM and the two passes below redo the tile with its
+        // true max (rescaling O and l as usual).
+        bool done = false;
+        if (j > 0 && !__any_sync(0xffffffffu, has_bias || has_mask)) {
+          const uint64_t mul2 = f2_pack(a.scale_log2, a.scale_log2);
+          const uint64_t neg2 = f2_pack(-m_run, -m_run);
+          uint64_t acc[4] = {0, 0, 0, 0};
+          uint32_t pk[2][32];
+          uint32_t rq[2][16];
+          tmem_ld16(t_s, rq[0]);
           tmem_wait_ld();
-          auto col = [&](int c) -> float {
-            return __uint_as_float(c < 32 ? rr[0][c] : r[(c >> 5) - 1][c & 31]);
-          };
-          // columns 0..3 start four chains, then 4..123 in steps of 8, then 124..127
-          float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
 #pragma unroll
-          for (int c = 4; c < 124; c += 8) {
-            mA = fmax3(mA, col(c), col(c + 1));
-            mB = fmax3(mB, col(c + 2), col(c + 3));
-            mC = fmax3(mC, col(c + 4), col(c + 5));
-            mD = fmax3(mD, col(c + 6), col(c + 7));
-          }
-          mA = fmax3(mA, col(124), col(125));
-          mB = fmax3(mB, col(126), col(127));
-          mul = a.scale_log2;
-          m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
-        } else {
-          float mx = -INFINITY;
+          for (int c = 0; c < 8; ++c) {
+            if (c < 7) tmem_ld16(t_s + (c + 1) * 16, rq[(c + 1) & 1]);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(t_s + c * 32, r);
-            tmem_wait_ld();
-            float x[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
-            // Relative bias, gathered by the whole warp: for each of the warp's 32 rows the
-            // lanes load that row's 32 consecutive values (one coalesced 64-byte access),
-            // store them to the transpose buffer, and each lane then reads its own row.
-            // Columns outside [bl, bh] (or rows without bias) read 0.
-            const bool chunk_bias = has_bias && c * 32 + 31 >= bl && c * 32 <= bh;
-            if (a.bias_vec) {
-              if (__any_sync(0xffffffffu, chunk_bias)) add_bias_window(bwin[c & 1], bh, c, x);
-              if (c < 2 && warp_bias)
-                load_bias_window(rel_row, bh, c + 2, a.rel_extent,
-                                 has_bias && (c + 2) * 32 + 31 >= bl && (c + 2) * 32 <= bh,
-                                 bwin[c & 1]);
-            } else if (__any_sync(0xffffffffu, chunk_bias)) {
-              uint16_t* buf = bias_buf;
-              const int col = c * 32 + lane;
-              uint16_t v[32];
-#pragma unroll
-              for (int tr = 0; tr < 32; ++tr) {  // all 32 loads in flight before any use
-                const int qi_t = qi - lane + tr;  // row of lane tr in this warp
-                const int d = qi_t + bs - k0 - col;
-                v[tr] = 0;
-                if (qi_t < sq && d >= 0 && d < a.rel_extent)
-                  v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
+            for (int i = 0; i < 8; ++i) {
+              const int col = c * 16 + 2 * i;
+              float y0, y1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(rq[c & 1][2 * i]),
+                                       __uint_as_float(rq[c & 1][2 * i + 1])),
+                               mul2, neg2),
+                        y0, y1);
+              float p0, p1;
+              if ((col & 15) < kEmu) {
+                exp2_poly_pair_capped(y0, y1, p0, p1);
+              } else if ((col & 15) < kEmu + kHalf2) {
+                exp2_h2_pair(y0, y1, p0, p1);  // fp16: >= 2^16 is inf, caught below
+              } else {
+                p0 = fast_exp2(y0);
+                p1 = fast_exp2(y1);
               }
-#pragma unroll
-              for (int tr = 0; tr < 32; ++tr) buf[tr * kBiasRowHalves + lane] = v[tr];
-              __syncwarp();
-              const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + lane * (kBiasRowHalves / 2);
-#pragma unroll
-              for (int k = 0; k < 16; ++k) {
-                const uint32_t pr = w[k];
-                x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
-                x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
-              }
-              __syncwarp();
+              acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
+              pk[c >> 2][(c & 3) * 8 + i] = pack_bf16x2(p0, p1);
             }
-            if (has_mask) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int col = c * 32 + i;
-                if (col < cl || col >= ch) x[i] = -INFINITY;
-              }
-            }
-            float m0 = x[0], m1 = x[1];
-#pragma unroll
-            for (int i = 2; i < 30; i += 4) {  // columns 2..29, then 30 and 31
-              m0 = fmax3(m0, x[i], x[i + 1]);
-              m1 = fmax3(m1, x[i + 2], x[i + 3]);
-            }
-            m0 = fmax3(m0, x[30], x[31]);
-            mx = fmax3(mx, m0, m1);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
-            __syncwarp();  // reconverge after the per-row branches: tcgen05.st is .aligned
-            tmem_st32(t_s + c * 32, r);
+            if (c < 7) tmem_wait_ld();
           }
-          tmem_wait_st();  // pass 2 reads these columns back
-          tmem_ld32(t_s, rr[0]);
-          tmem_wait_ld();
-          mul = 1.f;
-          m_tile = mx;
-        }
-        const float m_new = fmaxf(m_run, m_tile);
-        float alpha = 1.f;
-        bool need_rescale = false;
-        if (j == 0) {
-          m_run = m_new;
-        } else if (m_new > m_run + kRescaleThreshold) {
-          alpha = fast_exp2(m_run - m_new);
-          need_rescale = true;
-          l_run *= alpha;
-          m_run = m_new;
-        }
-        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
-        // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks (chunk 0 already in rr[0]),
-        // loading chunk c+1 while chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
-        // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
-        // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
-        const uint64_t mul2 = f2_pack(mul, mul);
-        const uint64_t neg2 = f2_pack(-m_use, -m_use);
-        uint64_t acc[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c * 32 + 2 * i;
-            float y0, y1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[c & 1][2 * i]),
-                                     __uint_as_float(rr[c & 1][2 * i + 1])),
-                             mul2, neg2),
-                      y0, y1);
-            float p0, p1;
-            if ((col & 15) < kEmu) {
-              exp2_poly_pair(y0, y1, p0, p1);
-            } else if ((col & 15) < kEmu + kHalf2) {
-              exp2_h2_pair(y0, y1, p0, p1);
-            } else {
-              p0 = fast_exp2(y0);
-              p1 = fast_exp2(y1);
-            }
-            acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
-            pk[i] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(t_s + c * 16, pk);
-          if (c < 3) tmem_wait_ld();
-        }
-        {
           const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
           float u0, u1;
           f2_unpack(f2_add(a01, a23), u0, u1);
-          l_run += u0 + u1;
+          const float l_tile = u0 + u1;
+          if (__all_sync(0xffffffffu, l_tile <= 4294967296.0f)) {  // false for inf and NaN
+            tmem_st32(t_s, pk[0]);
+            tmem_st32(t_s + 32, pk[1]);
+            l_run += l_tile;
+            done = true;
+          }
         }
-        // Conditional O correction (PV of the previous tile is complete: its commit
-        // preceded this tile's S commit).
-        if (__any_sync(0xffffffffu, need_rescale)) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(t_o + c * 32, o);
+        if (!done) {
+          // Pass 1 — the row max.  In a warp where no row needs bias or mask it is taken over the
+          // raw scores and the scale is folded into the exponent FMA (mul = scale*log2e).
+          // Otherwise every lane turns its scores into the scaled, biased, masked logit chunk by
+          // chunk and writes it back over S in TMEM, and pass 2 reads logits (mul = 1).
+          // Score chunk 0 (columns 0..31) is pass 2's first operand: in interior warps pass 1
+          // leaves it in rr[0], so pass 2 starts without a TMEM round trip.
+          uint32_t rr[2][32];
+          float mul, m_tile;
+          if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
+            uint32_t r[3][32];  // score chunks 1..3
+            tmem_ld32(t_s, rr[0]);
+  #pragma unroll
+            for (int c = 0; c < 3; ++c) tmem_ld32(t_s + (c + 1) * 32, r[c]);
             tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_o + c * 32, o);
+            auto col = [&](int c) -> float {
+              return __uint_as_float(c < 32 ? rr[0][c] : r[(c >> 5) - 1][c & 31]);
+            };
+            // columns 0..3 start four chains, then 4..123 in steps of 8, then 124..127
+            float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
+  #pragma unroll
+            for (int c = 4; c < 124; c += 8) {
+              mA = fmax3(mA, col(c), col(c + 1));
+              mB = fmax3(mB, col(c + 2), col(c + 3));
+              mC = fmax3(mC, col(c + 4), col(c + 5));
+              mD = fmax3(mD, col(c + 6), col(c + 7));
+            }
+            mA = fmax3(mA, col(124), col(125));
+            mB = fmax3(mB, col(126), col(127));
+            mul = a.scale_log2;
+            m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
+          } else {
+            float mx = -INFINITY;
+  #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(t_s + c * 32, r);
+              tmem_wait_ld();
+              float x[32];
+  #pragma unroll
+              for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
+              // Relative bias, gathered by the whole warp: for each of the warp's 32 rows the
+              // lanes load that row's 32 consecutive values (one coalesced 64-byte access),
+              // store them to the transpose buffer, and each lane then reads its own row.
+              // Columns outside [bl, bh] (or rows without bias) read 0.
+              const bool chunk_bias = has_bias && c * 32 + 31 >= bl && c * 32 <= bh;
+              if (a.bias_vec) {
+                if (__any_sync(0xffffffffu, chunk_bias)) add_bias_window(bwin[c & 1], bh, c, x);
+                if (c < 2 && warp_bias)
+                  load_bias_window(rel_row, bh, c + 2, a.rel_extent,
+                                   has_bias && (c + 2) * 32 + 31 >= bl && (c + 2) * 32 <= bh,
+                                   bwin[c & 1]);
+              } else if (__any_sync(0xffffffffu, chunk_bias)) {
+                uint16_t* buf = bias_buf;
+                const int col = c * 32 + lane;
+                uint16_t v[32];
+  #pragma unroll
+                for (int tr = 0; tr < 32; ++tr) {  // all 32 loads in flight before any use
+                  const int qi_t = qi - lane + tr;  // row of lane tr in this warp
+                  const int d = qi_t + bs - k0 - col;
+                  v[tr] = 0;
+                  if (qi_t < sq && d >= 0 && d < a.rel_extent)
+                    v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
+                }
+  #pragma unroll
+                for (int tr = 0; tr < 32; ++tr) buf[tr * kBiasRowHalves + lane] = v[tr];
+                __syncwarp();
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + lane * (kBiasRowHalves / 2);
+  #pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                  const uint32_t pr = w[k];
+                  x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
+                  x[2 * k + 1] += __uint_as_float(pr & 0xffff0000u) * kLog2e;
+                }
+                __syncwarp();
+              }
+              if (has_mask) {
+  #pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const int col = c * 32 + i;
+                  if (col < cl || col >= ch) x[i] = -INFINITY;
+                }
+              }
+              float m0 = x[0], m1 = x[1];
+  #pragma unroll
+              for (int i = 2; i < 30; i += 4) {  // columns 2..29, then 30 and 31
+                m0 = fmax3(m0, x[i], x[i + 1]);
+                m1 = fmax3(m1, x[i + 2], x[i + 3]);
+              }
+              m0 = fmax3(m0, x[30], x[31]);
+              mx = fmax3(mx, m0, m1);
+  #pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
+              __syncwarp();  // reconverge after the per-row branches: tcgen05.st is .aligned
+              tmem_st32(t_s + c * 32, r);
+            }
+            tmem_wait_st();  // pass 2 reads these columns back
+            tmem_ld32(t_s, rr[0]);
+            tmem_wait_ld();
+            mul = 1.f;
+            m_tile = mx;
+          }
+          const float m_new = fmaxf(m_run, m_tile);
+          float alpha = 1.f;
+          bool need_rescale = false;
+          if (j == 0) {
+            m_run = m_new;
+          } else if (m_new > m_run + kRescaleThreshold) {
+            alpha = fast_exp2(m_run - m_new);
+            need_rescale = true;
+            l_run *= alpha;
+            m_run = m_new;
+          }
+          const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+          __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
+          // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks (chunk 0 already in rr[0]),
+          // loading chunk c+1 while chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
+          // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
+          // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
+          const uint64_t mul2 = f2_pack(mul, mul);
+          const uint64_t neg2 = f2_pack(-m_use, -m_use);
+          uint64_t acc[4] = {0, 0, 0, 0};
+  #pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
+            uint32_t pk[16];
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = c * 32 + 2 * i;
+              float y0, y1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[c & 1][2 * i]),
+                                       __uint_as_float(rr[c & 1][2 * i + 1])),
+                               mul2, neg2),
+                        y0, y1);
+              float p0, p1;
+              if ((col & 15) < kEmu) {
+                exp2_poly_pair(y0, y1, p0, p1);
+              } else if ((col & 15) < kEmu + kHalf2) {
+                exp2_h2_pair(y0, y1, p0, p1);
+              } else {
+                p0 = fast_exp2(y0);
+                p1 = fast_exp2(y1);
+              }
+              acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
+              pk[i] = pack_bf16x2(p0, p1);
+            }
+            tmem_st16(t_s + c * 16, pk);
+            if (c < 3) tmem_wait_ld();
+          }
+          {
+            const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+            float u0, u1;
+            f2_unpack(f2_add(a01, a23), u0, u1);
+            l_run += u0 + u1;
+          }
+          // Conditional O correction (PV of the previous tile is complete: its commit
+          // preceded this tile's S commit).
+          if (__any_sync(0xffffffffu, need_rescale)) {
+  #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t o[32];
+              tmem_ld32(t_o + c * 32, o);
+              tmem_wait_ld();
+  #pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(t_o + c * 32, o);
+            }
           }
         }
         // every lane's TMEM stores are complete and fenced before lane 0 releases P

@@ -450,6 +450,13 @@ __device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, fl
   y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
+// exp2_poly_pair with the inputs also capped at 64 (result <= 2^64): for callers whose
+// arguments may exceed 127, where the exponent insertion above would wrap; a capped result is
+// still far above anything they accept, so the cap never changes an accepted value.
+__device__ __forceinline__ void exp2_poly_pair_capped(float x0, float x1, float& y0, float& y1) {
+  exp2_poly_pair(fminf(x0, 64.0f), fminf(x1, 64.0f), y0, y1);
+}
+
 // 2^x for a pair of floats with one SFU instruction (ex2.approx.f16x2): the inputs are rounded
 // to fp16 (10-bit mantissa; the arguments are <= 8 here, so the input rounding changes the
 // result by at most 0.14 %, below the bf16 rounding applied to it next) and the fp16 results

@@ -172,6 +172,29 @@ def test_tile_config_variants_match_oracle(tile_config):
     assert_close(np32(got), np32(ref), atol=1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("scale", [60.0, 400.0, 3000.0])
+@pytest.mark.parametrize("tile_config", [1, 3, 6])
+def test_scores_far_above_the_running_max(scale, tile_config):
+    """Interior tiles take their exponentials against the running max without a row-max pass
+    and keep the tile only if its sum of p stays <= 2^32.  Keys scaled up from position 1000 on
+    push scores 2^30 (x60) to far beyond 2^128 (x400, x3000) above that max: the tile must then
+    be redone with its true max (SFU, FMA-pipe polynomial and fp16 SFU exponentials alike)."""
+    from inkling_fa4.workloads import Case
+    c = make_case([2048, 1500], [2048, 1500], 4, 2, 128, seed=int(scale))
+    k = c.k.float()
+    k[1000:2048] *= scale
+    k[2048 + 700:] *= scale
+    c = Case(q=c.q, k=k.to(torch.bfloat16), v=c.v, rel=c.rel, cu_q=c.cu_q, cu_k=c.cu_k,
+             seqlens_q=c.seqlens_q, seqlens_k=c.seqlens_k, rel_extent=128)
+    c = to_dev(c)
+    toks, want = oracle_rows(c, 48, list(range(4)), 1 / 128, seed=int(scale) + 1)
+    from inkling_fa4 import _ops
+    out, lse = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, c.max_q, c.max_k, 128,
+                            tile_config=tile_config, return_lse=True)
+    assert_close(np32(out)[toks], want, what=f"tile_config {tile_config}")
+    assert torch.isfinite(lse).all() and torch.isfinite(out.float()).all()
+
+
 def test_window_row_without_keys_is_zero_in_default_config():
     # bottom-right chunk shorter than a window gap: early query rows see no key at all
     c = to_dev(make_case([64], [64], 4, 4, 64, seed=13))
