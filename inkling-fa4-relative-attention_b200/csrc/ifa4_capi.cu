@@ -293,7 +293,7 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   if (ifa4::prefill_emulated_exp_columns(p->tile_config) < 0)
     return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d unknown", p->tile_config);
   if (p->block_table != nullptr && !ifa4::prefill_paged_tile_config_ok(p->tile_config))
-    return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d has no paged-cache variant (0, 1, 3)",
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d has no paged-cache variant (0 to 3)",
                 p->tile_config);
   if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
   int* status = nullptr;

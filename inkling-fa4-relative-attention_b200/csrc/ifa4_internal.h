@@ -52,16 +52,15 @@ struct PrefillLaunch {
 
 // Prefill tile configurations: the kernel variants differ in where the exponentials of every 16
 // score columns are computed: FMA-pipe polynomial, SFU two-at-a-time (f16x2), or SFU fp32.
-// tile_config 0 = automatic (4 polynomial columns of 16 for sequences >= 16k without a
-// sliding window, none otherwise); 1..5 = 0, 2, 4, 6, 8 polynomial columns of 16; 6 = all f16x2; 7 = 8 of 16 f16x2;
+// tile_config 0 = automatic (2 polynomial columns of 16); 1..5 = 0, 2, 4, 6, 8 polynomial columns of 16; 6 = all f16x2; 7 = 8 of 16 f16x2;
 // 8 = 4 polynomial + 8 f16x2.
-constexpr int kPrefillDefaultEmu = 0;
+constexpr int kPrefillDefaultEmu = 2;
 constexpr int kPrefillDefaultHalf2 = 0;
 constexpr int kPrefillNumTileConfigs = 9;
 int prefill_emulated_exp_columns(int tile_config);  // -1 for an unknown id
 
 // Launches the tcgen05 prefill kernel variant of `tile_config`.  Returns a cudaError_t.
-// With a paged cache (args.block_table != nullptr) only tile configs 0, 1 and 3 exist.
+// With a paged cache (args.block_table != nullptr) only tile configs 0 to 3 exist.
 cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                  int q_slots, int tile_config, int max_seqlen_q,

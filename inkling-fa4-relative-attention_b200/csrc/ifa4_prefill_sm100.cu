@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!__any_sync(0xffffffffu, has_bias || has_mask)) {
             uint32_t r[3][32];  // score chunks 1..3
             tmem_ld32(t_s, rr[0]);
-  #pragma unroll
+#pragma unroll
             for (int c = 0; c < 3; ++c) tmem_ld32(t_s + (c + 1) * 32, r[c]);
             tmem_wait_ld();
             auto col = [&](int c) -> float {
@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             // columns 0..3 start four chains, then 4..123 in steps of 8, then 124..127
             float mA = col(0), mB = col(1), mC = col(2), mD = col(3);
-  #pragma unroll
+#pragma unroll
             for (int c = 4; c < 124; c += 8) {
               mA = fmax3(mA, col(c), col(c + 1));
               mB = fmax3(mB, col(c + 2), col(c + 3));
@@ -593,13 +593,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_tile = fmax3(mA, mB, fmaxf(mC, mD)) * mul;
           } else {
             float mx = -INFINITY;
-  #pragma unroll
+#pragma unroll
             for (int c = 0; c < 4; ++c) {
               uint32_t r[32];
               tmem_ld32(t_s + c * 32, r);
               tmem_wait_ld();
               float x[32];
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]) * a.scale_log2;
               // Relative bias, gathered by the whole warp: for each of the warp's 32 rows the
               // lanes load that row's 32 consecutive values (one coalesced 64-byte access),
@@ -616,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint16_t* buf = bias_buf;
                 const int col = c * 32 + lane;
                 uint16_t v[32];
-  #pragma unroll
+#pragma unroll
                 for (int tr = 0; tr < 32; ++tr) {  // all 32 loads in flight before any use
                   const int qi_t = qi - lane + tr;  // row of lane tr in this warp
                   const int d = qi_t + bs - k0 - col;
@@ -624,11 +624,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (qi_t < sq && d >= 0 && d < a.rel_extent)
                     v[tr] = __ldg(rel_row + static_cast<long long>(tr - lane) * a.rel_st + d);
                 }
-  #pragma unroll
+#pragma unroll
                 for (int tr = 0; tr < 32; ++tr) buf[tr * kBiasRowHalves + lane] = v[tr];
                 __syncwarp();
                 const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + lane * (kBiasRowHalves / 2);
-  #pragma unroll
+#pragma unroll
                 for (int k = 0; k < 16; ++k) {
                   const uint32_t pr = w[k];
                   x[2 * k] += __uint_as_float(pr << 16) * kLog2e;
@@ -637,21 +637,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
               }
               if (has_mask) {
-  #pragma unroll
+#pragma unroll
                 for (int i = 0; i < 32; ++i) {
                   const int col = c * 32 + i;
                   if (col < cl || col >= ch) x[i] = -INFINITY;
                 }
               }
               float m0 = x[0], m1 = x[1];
-  #pragma unroll
+#pragma unroll
               for (int i = 2; i < 30; i += 4) {  // columns 2..29, then 30 and 31
                 m0 = fmax3(m0, x[i], x[i + 1]);
                 m1 = fmax3(m1, x[i + 2], x[i + 3]);
               }
               m0 = fmax3(m0, x[30], x[31]);
               mx = fmax3(mx, m0, m1);
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(x[i]);
               __syncwarp();  // reconverge after the per-row branches: tcgen05.st is .aligned
               tmem_st32(t_s + c * 32, r);
@@ -676,33 +676,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
           __syncwarp();  // reconverge: the tcgen05 operations below are .sync.aligned
           // Pass 2 — p = 2^(x * mul - m_use) over 32-column chunks (chunk 0 already in rr[0]),
-          // loading chunk c+1 while chunk c is computed.  Of every 16 columns kEmu use the FMA-pipe polynomial, kHalf2 the
-          // SFU two at a time (f16x2), the rest the SFU in fp32.  P (bf16 pairs) goes to TMEM
-          // columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1)) never overlap.
+          // loading chunk c+1 while chunk c is computed.  All exponentials on the SFU in fp32
+          // (this path carries the masked tiles, whose -inf logits must give exactly 0; the
+          // FMA-pipe and f16x2 variants apply to the single-pass interior path above).  P (bf16
+          // pairs) goes to TMEM columns [16c, 16c+16), which chunks c+1.. (columns >= 32(c+1))
+          // never overlap.
           const uint64_t mul2 = f2_pack(mul, mul);
           const uint64_t neg2 = f2_pack(-m_use, -m_use);
           uint64_t acc[4] = {0, 0, 0, 0};
-  #pragma unroll
+#pragma unroll
           for (int c = 0; c < 4; ++c) {
             if (c < 3) tmem_ld32(t_s + (c + 1) * 32, rr[(c + 1) & 1]);
             uint32_t pk[16];
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const int col = c * 32 + 2 * i;
               float y0, y1;
               f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[c & 1][2 * i]),
                                        __uint_as_float(rr[c & 1][2 * i + 1])),
                                mul2, neg2),
                         y0, y1);
-              float p0, p1;
-              if ((col & 15) < kEmu) {
-                exp2_poly_pair(y0, y1, p0, p1);
-              } else if ((col & 15) < kEmu + kHalf2) {
-                exp2_h2_pair(y0, y1, p0, p1);
-              } else {
-                p0 = fast_exp2(y0);
-                p1 = fast_exp2(y1);
-              }
+              const float p0 = fast_exp2(y0), p1 = fast_exp2(y1);
               acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
               pk[i] = pack_bf16x2(p0, p1);
             }
@@ -718,12 +711,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Conditional O correction (PV of the previous tile is complete: its commit
           // preceded this tile's S commit).
           if (__any_sync(0xffffffffu, need_rescale)) {
-  #pragma unroll
+#pragma unroll
             for (int c = 0; c < 4; ++c) {
               uint32_t o[32];
               tmem_ld32(t_o + c * 32, o);
               tmem_wait_ld();
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
               tmem_st32(t_o + c * 32, o);
             }
@@ -743,8 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait_warp(&bars->o_full[s], oc & 1, ab))) break;
       ++oc;
       tc_fence_after();
-      // a row that never saw a visible key outputs 0 (the FMA-pipe exp2 of a masked
-      // logit is ~2^-125, not 0, so l alone does not tell)
+      // a row that never saw a visible key outputs 0 (its running max is still -inf)
       const bool seen = l_run > 0.f && m_run != -INFINITY;
       const float inv_l = seen ? 1.f / l_run : 0.f;
       if (a.lse != nullptr && row_valid)  // ln(sum exp) = ln2 * (m + log2 l) in the exp2 domain
@@ -837,7 +829,7 @@ static const int kVariants[kPrefillNumTileConfigs][2] = {
     {0, 16}, {0, 8}, {4, 8}};
 
 bool prefill_paged_tile_config_ok(int tile_config) {
-  return tile_config == 0 || tile_config == 1 || tile_config == 3;
+  return tile_config >= 0 && tile_config <= 3;
 }
 
 int prefill_emulated_exp_columns(int tile_config) {
@@ -855,15 +847,16 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
   if (tile_config < 0 || tile_config >= kPrefillNumTileConfigs) return cudaErrorInvalidValue;
   int emu = kVariants[tile_config][0], h2 = kVariants[tile_config][1];
   if (tile_config == 0) {
-    // Measured on B200 (interleaved A/B, GQA 32/8): on long causal sequences the SFU is the
-    // softmax bottleneck and 4 of 16 exponentials on the FMA pipe win (32k: 975 vs 921
-    // TFLOP/s); with a 4096 window (boundary tiles dominate) or on short ragged sequences
-    // (<= 4k: 425 vs 458) the all-SFU variant wins.
-    emu = (args.window_left < 0 && max_seqlen_q >= 16384) ? 4 : 0;
+    // Measured on B200 (interleaved A/B, GQA 32/8, R = 128): with interior tiles taking their
+    // exponentials against the running max (no row-max pass), 2 FMA-pipe exponentials of 16
+    // beat all-SFU by 0.5 % (32k causal), 3.6 % (window 4096) and 1.6 % (ragged), and 4 of 16
+    // lose 4 % at 32k.
+    emu = 2;
     h2 = 0;
   }
-  if (args.block_table != nullptr) {  // paged cache: the two variants the automatic choice uses
+  if (args.block_table != nullptr) {  // paged cache: the automatic choice and its neighbours
     if (emu == 0 && h2 == 0) return launch_variant<0, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
+    if (emu == 2 && h2 == 0) return launch_variant<2, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
     if (emu == 4 && h2 == 0) return launch_variant<4, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);
     return cudaErrorInvalidValue;
   }

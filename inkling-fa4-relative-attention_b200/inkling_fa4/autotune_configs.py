@@ -29,7 +29,7 @@ PRESETS = {
 # bench.py --only prefill (32k causal, GQA 32/8): TFLOP/s per variant.  tile_config 0 resolves
 # to the fastest.
 TILE_CONFIGS = {
-    0: {"note": "automatic: tile_config 3 for max_seqlen_q >= 16384 without a window, else 1"},
+    0: {"note": "automatic: tile_config 2 (2 FMA-pipe exponentials of 16)"},
     1: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 0},
     2: {"emulated_exp_of_16": 2, "sfu_f16x2_of_16": 0},
     3: {"emulated_exp_of_16": 4, "sfu_f16x2_of_16": 0},
@@ -39,10 +39,12 @@ TILE_CONFIGS = {
     7: {"emulated_exp_of_16": 0, "sfu_f16x2_of_16": 8},
     8: {"emulated_exp_of_16": 4, "sfu_f16x2_of_16": 8},
 }
-# Interleaved A/B on one B200 (7 rounds x 5 calls, medians), 32k GQA 32/8, TFLOP/s:
-#   causal:      tc1 920.8  tc3 974.7  tc6 873.3  tc7 934.8  tc8 936.0
-#   window 4096: tc1 776.2  tc3 759.0  tc6 710.3  tc7 762.5  tc8 740.5
-# ragged (config 2, <= 4k tokens): all-SFU 458 vs tc3 425.
+# Interleaved A/B on one B200 (5 rounds, medians), GQA 32/8, R = 128, TFLOP/s, with interior
+# tiles taking their exponentials against the running max (no row-max pass):
+#   causal 32k:   tc1 1034.6  tc2 1039.8  tc3 993.5  tc7 1011.7  tc8 973.5
+#   window 4096:  tc1  863.3  tc2  894.2  tc3 862.8  tc7  859.2  tc8 850.0
+#   ragged (config 2): tc1 597.3  tc2 606.6  tc3 585.1  tc7 598.0  tc8 563.7
+# Paged caches: tile configs 0 to 3.
 DECODE_PRESET = {"BLOCK_K": 64, "num_warps": 5, "num_stages": 3, "chunk_len": 0, "num_splits": 0}
 
 

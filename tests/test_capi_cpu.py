@@ -160,7 +160,7 @@ def _paged_params(**kw):
     (dict(block_table_stride=-1), _lib.IFA4_ERR_INVALID_ARGUMENT, b"block_table_stride"),
     (dict(k_stride_page=4), _lib.IFA4_ERR_INVALID_ARGUMENT, b"page strides"),
     (dict(v_stride_page=0), _lib.IFA4_ERR_INVALID_ARGUMENT, b"page strides"),
-    (dict(tile_config=2), _lib.IFA4_ERR_UNSUPPORTED, b"paged"),
+    (dict(tile_config=4), _lib.IFA4_ERR_UNSUPPORTED, b"paged"),
 ])
 def test_paged_cache_validation(kw, code, msg):
     L = _lib.lib()
