@@ -314,11 +314,15 @@ def main():
 
     from inkling_fa4 import _ops
 
-    def prefill_step():
+    def prefill_call(*pa, **kw):
+        """The public prefill entry point, or the same call pinned to --tile-config (for tile
+        sweeps; applies to the headline, window, ragged and chunked legs)."""
         if args.tile_config:
-            return _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R,
-                                tile_config=args.tile_config)
-        return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R)
+            return _ops.prefill(*pa, tile_config=args.tile_config, **kw)
+        return inkling_fa4_rel_attention_triton(*pa, **kw)
+
+    def prefill_step():
+        return prefill_call(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R)
 
     uuids = []
     try:
@@ -443,8 +447,8 @@ def main():
         wflops = 4 * D * HQ * visible_pairs_causal(S, 4096)
 
         def win_step():
-            return inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S,
-                                                    R, window_size=(4096, 0))
+            return prefill_call(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R,
+                                window_size=(4096, 0))
 
         wms = timed(win_step, args.steps, args.warmup, stream, dist, barrier)
         result["window32k"] = {"value": world * wflops * args.steps / (wms / 1e3) / 1e12,
@@ -568,9 +572,8 @@ def main():
                                                    causal_align=align)
 
             def step(cc=cc, align=align):
-                return inkling_fa4_rel_attention_triton(cc.q, cc.k, cc.v, cc.rel, cc.cu_q,
-                                                        cc.cu_k, cc.max_q, cc.max_k, R,
-                                                        causal_align=align)
+                return prefill_call(cc.q, cc.k, cc.v, cc.rel, cc.cu_q, cc.cu_k, cc.max_q,
+                                    cc.max_k, R, causal_align=align)
 
             xms = timed(step, args.steps, args.warmup, stream, dist, barrier)
             result[name] = {"value": world * fl * args.steps / (xms / 1e3) / 1e12,
@@ -581,8 +584,12 @@ def main():
                 pc = page_kv(cc, page_size=16, seed=rank)
                 del cc
 
+                # paged caches exist for tile configs 0 to 3; other sweep values run the default
+                paged_call = prefill_call if args.tile_config <= 3 else \
+                    inkling_fa4_rel_attention_triton
+
                 def pstep(pc=pc):
-                    return inkling_fa4_rel_attention_triton(
+                    return paged_call(
                         pc.q, pc.k, pc.v, pc.rel, pc.cu_q, pc.cu_k, pc.max_q, pc.max_k, R,
                         causal_align="bottom_right", block_table=pc.meta["block_table"])
 
