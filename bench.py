@@ -74,6 +74,27 @@ def visible_pairs_causal(seq, window=None):
     return w * (w + 1) // 2 + full * w if seq >= w else seq * (seq + 1) // 2
 
 
+class c_stdout_to_stderr:
+    """Point file descriptor 1 at stderr for the duration (C-level writes included)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        try:
+            import ctypes
+            ctypes.CDLL(None).fflush(None)  # C stdio buffers written inside go to stderr too
+        except OSError:
+            pass
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        return False
+
+
 # ---------------------------------------------------------------------------------------
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
@@ -294,8 +315,14 @@ def main():
 
         import torch.distributed as tdist
 
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                 device_id=torch.device("cuda", local_rank))
+        # NCCL prints its version banner (with NCCL_DEBUG set) on the process's C stdout when the
+        # communicator is created, and debug lines to its debug file (stdout by default); rank 0's
+        # stdout must hold only the JSON result line, so both go to stderr.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        with c_stdout_to_stderr():
+            tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                     device_id=torch.device("cuda", local_rank))
+            tdist.barrier()  # the communicator exists (and has printed) before stdout returns
         dist = tdist
     barrier = (lambda: dist.barrier()) if dist else None
 
