@@ -6,31 +6,41 @@
 
 Headline (``value``): prefill TFLOP/s on the 32k causal GQA 32/8, d=128, R=128 configuration
 (full causal), aggregated over all ranks.  A "step" is one prefill call over
-one 32768-token sequence with all 32 query heads.  FLOPs are algorithmic:
-4 * head_dim * n_heads * (causally visible query/key pairs), the bias gather and masking
-excluded.  Scaling is weak: every rank owns an independent 32k sequence (work shards by
-sequence / KV-head group with no data-path collective); ``value`` = all ranks' FLOPs / the
-slowest rank's time.
+one 32768-token sequence with all 32 query heads; exactly K steps are timed after W warm-up
+steps.  FLOPs are algorithmic: 4 * head_dim * n_heads * (visible query/key pairs), the bias
+gather and masking excluded.  Scaling is weak: every rank owns an independent 32k sequence
+(work shards by sequence / KV-head group with no data-path collective); ``value`` = all ranks'
+FLOPs / the slowest rank's time.
 
-Secondary objects in the same JSON line: the sliding-window variant (window 4096), the backward,
-the rel_logits producer for the headline shape (GB/s against HBM), batched
-decode (GB/s and us/step against HBM), the end-to-end number through the
-public API with host buffers (``e2e``), the CPU baseline (the oracle on host cores, bounded
-sample) and SM clocks sampled during the timed region.
+Every other BASELINE configuration is a secondary object of the same JSON line, each with its
+roofline fraction and, at N = 1, its CPU baseline (the oracle, on a bounded sample):
+config 1 (S=128, Hq=Hkv=4, scale 1/sqrt(128), per-head distance table), config 2 (ragged
+16 x U[1, 4096]), config 3b (window 4096), config 4 (chunked 8 x (16384 + 2048), contiguous
+and paged), config 5 (batched decode, contiguous and paged, GB/s against HBM); plus the shapes
+the reference itself benchmarks and the model uses (R = 1024 global layer, R = 512 with window
+511 local layer, and the reference benchmark's own S=4096 Hq=Hkv=4 R=1024 shape), the
+backward, the rel_logits producer, and the end-to-end number through the public API with host
+buffers (``e2e``).  Secondary legs time max(K, 50) steps after max(W, 10) warm-up steps and
+report the median step as well as the mean.  SM clocks are sampled with nvidia-smi from the
+headline's warm-up to the end of the last GPU leg.
+
+At N > 1 two more legs split ONE problem over the ranks by KV-head group (strong scaling):
+the 32k prefill and the config-5 decode, each timed without and with the all-gather of the
+output heads, and each checked against the rank's own unsharded call (``parity_ok``).
 
 ``--impl reference`` times the reference's algorithm on the host CPU (the oracle port; the
-reference itself is a Python/Triton package whose CPU path is the torch oracle ref_rel_attn),
-on bounded samples of the same workload; rank 0 only.
+reference itself is a Python/Triton package whose CPU path is the torch oracle ref_rel_attn)
+on the same bounded sample as the headline's ``cpu_baseline``; rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -39,7 +49,26 @@ sys.path.insert(0, ROOT)
 
 METRIC = "prefill TFLOP/s at 32k GQA 32/8 d128 bf16; decode HBM GB/s & us/step"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DATASHEET = {"bf16_tflops": 2250.0, "hbm_gbs": 7700.0}
 SEQ, HQ, HKV, D, R = 32768, 32, 8, 128, 128
+# Published latency of the reference on its own benchmark shape (S=4096, Hq=Hkv=4, d=128,
+# R=1024, causal; RTX 3090, after tuning): README.md:14 of the reference.
+REF_PUBLISHED_MS_S4096 = 1.037
+
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one-pass ncu
+# captures of this script's own workloads (command:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+#       --clock-control none -k regex:<kernel> -s 3 -c 1 python bench.py --only <leg> ...).
+# The decode figure is a batch-16 capture (1.0066 x its algorithmic bytes) scaled to the
+# batch-128 step by K/V bytes; the others are full-size launches.
+NCU_DRAM_BYTES_PER_LAUNCH = {
+    "prefill_causal32k": 951016448,
+    "rel_logits32k": 248236032,
+    "decode128": 9576854379,
+}
+
+LEGS = ("e2e", "window", "ragged", "chunked", "global_rel1024", "local_rel512",
+        "refbench", "config1", "backward", "rel_logits", "decode")
 
 
 def load_peaks():
@@ -49,21 +78,6 @@ def load_peaks():
             j = json.load(f)
         return {k: float(j[k]) for k in FALLBACK_PEAKS}, "measured"
     return dict(FALLBACK_PEAKS), "fallback"
-
-
-def profile_traffic(name):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name> (a line
-    'dram_bytes_per_launch_full: <int>'), or None."""
-    p = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(p):
-        return None
-    for line in open(p):
-        if line.startswith("dram_bytes_per_launch_full:"):
-            try:
-                return int(float(line.split(":", 1)[1].strip()))
-            except ValueError:
-                return None
-    return None
 
 
 def visible_pairs_causal(seq, window=None):
@@ -97,7 +111,7 @@ class c_stdout_to_stderr:
 
 # ---------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU legs run."""
 
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -107,19 +121,21 @@ class ClockSampler:
         self.uuids = [u.lower() for u in uuids]
         self.proc = None
         self.lines = []
+        self.first = threading.Event()
 
     def _drain(self):
         for line in self.proc.stdout:
             self.lines.append(line)
+            self.first.set()
 
-    def start(self):
-        import threading
+    def start(self, wait_s=3.0):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._drain, daemon=True)
             self.reader.start()
+            self.first.wait(wait_s)  # sampling has begun before the timed work starts
         except Exception:
             self.proc = None
 
@@ -143,84 +159,243 @@ class ClockSampler:
             rows.append(parts)
         if not rows:
             return None
-        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        smax = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
-        pw = [float(r[4]) for r in rows if r[4].replace(".", "").isdigit()]
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [num(r[2]) for r in rows]
+        pw = [num(r[4]) for r in rows]
+        smax = [x for x in (num(r[3]) for r in rows) if x is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
-        loaded = [s for s, p in zip(sm, pw) if p > 300] or sm
+        loaded_rows = [i for i, p in enumerate(pw) if p is not None and p > 300]
+        reasons = sorted({names[i] for k in (loaded_rows or range(len(rows)))
+                          for i in range(4) if rows[k][6 + i].lower() == "active"})
+        loaded = [sm[i] for i in loaded_rows if sm[i] is not None] or \
+            [x for x in sm if x is not None]
         return {"sm_mhz": statistics.median(loaded) if loaded else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(pw) if pw else None}
+                "samples": len(rows), "samples_under_load": len(loaded_rows),
+                "power_w_max": max((p for p in pw if p is not None), default=None),
+                "window": "from the headline's warm-up to the end of the last GPU leg"}
 
 
 # ---------------------------------------------------------------------------------------
-def cpu_baseline_prefill(seconds, window=None, threads=None):
-    """The oracle (torch twin of reference.py's algorithm, all host threads) on a bounded
-    sample of the 32k workload: one head, 128-row blocks spread over the sequence, each row
-    scored densely against all keys as the reference does.  Returns (TFLOP/s, cores, sample)."""
-    import torch
+# CPU baselines: the torch-CPU twin of reference.py's algorithm (the oracle port), all host
+# threads, on bounded samples of each configuration.  Inputs have the configuration's shapes
+# and distributions (seeded, generated on the CPU); every sample scores its rows densely
+# against all keys, as reference.py computes them, and is credited with algorithmic FLOPs
+# (or bytes) only.
 
-    import oracle
-    from inkling_fa4.workloads import make_case
-
-    threads = threads or os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    c = make_case([SEQ], [SEQ], 1, 1, R, seed=123, rel_std=0.5)
-    q, k, v, rel = (t[:, 0].float().contiguous() for t in (c.q, c.k, c.v, c.rel))
-    blk = 128
-    order = [((i * 97) % (SEQ // blk)) * blk for i in range(SEQ // blk)]
-    flops, t_used, rows = 0, 0.0, 0
-    for r0 in order:
-        t0 = time.perf_counter()
-        oracle.rel_attn_rows_torch(q[r0:r0 + blk], k, v, rel[r0:r0 + blk],
-                                   torch.arange(r0, r0 + blk), SEQ, SEQ, 1.0 / D, R, True,
-                                   window, "reference")
-        t_used += time.perf_counter() - t0
-        for i in range(r0, r0 + blk):
-            lo = 0 if window is None else max(0, i - window)
-            flops += 4 * D * (i + 1 - lo)
-        rows += blk
-        if t_used >= seconds:
-            break
-    sample = (f"1 of {HQ} heads, {rows} of {SEQ} query rows ({rows // blk} blocks of {blk} "
-              f"spread over the sequence), dense scores against all {SEQ} keys as reference.py "
-              "computes them; algorithmic causal FLOPs")
-    return flops / t_used / 1e12, threads, sample
-
-
-def run_reference_arm(args, rank, world):
-    if rank != 0:
-        return
+def _cpu_threads():
     import torch
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
+    return threads
+
+
+class CausalSample:
+    """The headline's CPU sample: one head of the 32k causal sequence, 128-row blocks taken in
+    a fixed order spread over the sequence (block i at rows ((97 i) mod 256) * 128)."""
+
+    BLK = 128
+
+    def __init__(self, window=None):
+        from inkling_fa4.workloads import make_case
+
+        c = make_case([SEQ], [SEQ], 1, 1, R, seed=123, rel_std=0.5)
+        self.q, self.k, self.v, self.rel = (t[:, 0].float().contiguous()
+                                            for t in (c.q, c.k, c.v, c.rel))
+        self.window = window
+        self.n_blocks = SEQ // self.BLK
+
+    def block(self, i):
+        """Run block i; returns (its algorithmic FLOPs, seconds)."""
+        import torch
+
+        import oracle
+
+        r0 = ((i * 97) % self.n_blocks) * self.BLK
+        lo = lambda r: 0 if self.window is None else max(0, r - self.window)
+        flops = sum(4 * D * (r + 1 - lo(r)) for r in range(r0, r0 + self.BLK))
+        pos = torch.arange(r0, r0 + self.BLK)
+        return _clocked(lambda: oracle.rel_attn_rows_torch(
+            self.q[r0:r0 + self.BLK], self.k, self.v, self.rel[r0:r0 + self.BLK], pos, SEQ, SEQ,
+            1.0 / D, R, True, self.window, "reference"), flops)
+
+    def describe(self, blocks):
+        w = "" if self.window is None else f", window {self.window}"
+        return (f"1 of {HQ} heads, {blocks * self.BLK} of {SEQ} query rows ({blocks} blocks of "
+                f"{self.BLK} spread over the sequence{w}), dense scores against all {SEQ} keys as "
+                "reference.py computes them; algorithmic FLOPs")
+
+
+def _run_for(seconds, fn, start=0):
+    """Call fn(i) for i = start, start+1, ... until `seconds` of timed CPU work; fn returns
+    (units of work, seconds it timed), so input preparation stays outside the count.  Returns
+    (total units, seconds, calls)."""
+    units, used, i = 0, 0.0, start
+    while used < seconds:
+        u, dt = fn(i)
+        units += u
+        used += dt
+        i += 1
+    return units, used, i - start
+
+
+def _clocked(run, units):
+    t0 = time.perf_counter()
+    run()
+    return units, time.perf_counter() - t0
+
+
+def cpu_causal32k(seconds, window=None):
+    threads = _cpu_threads()
+    s = CausalSample(window)
+    s.block(0)  # warm-up (thread pool, allocator)
+    flops, used, n = _run_for(seconds, s.block, start=1)
+    return {"value": flops / used / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": s.describe(n), "seconds": used}
+
+
+def cpu_config1(seconds):
+    """Config 1 in full (S=128, Hq=Hkv=4, scale 1/sqrt(128), per-head table), repeated."""
+    import oracle
+    from inkling_fa4.workloads import config_cpu_reference
+
+    threads = _cpu_threads()
+    c = config_cpu_reference()
+    args = [t.float() for t in (c.q, c.k, c.v, c.rel)]
+    fl = 4 * D * 4 * visible_pairs_causal(128)
+
+    def call(_):
+        return _clocked(lambda: oracle.rel_attn_torch(*args, c.cu_q, c.cu_k, 128 ** -0.5, 128), fl)
+
+    call(0)
+    flops, used, n = _run_for(seconds, call)
+    return {"value": flops / used / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "ms_per_call": used * 1e3 / n, "sample": f"the whole configuration, {n} calls"}
+
+
+def cpu_ragged(seconds):
+    """Config 2: (sequence, head) pairs of the seeded ragged batch in a fixed order, each a
+    full dense per-head attention of that sequence."""
+    import torch
+
+    import oracle
+    from inkling_fa4.workloads import make_case, ragged_batch_lengths
+
+    threads = _cpu_threads()
+    lens = ragged_batch_lengths()
+    cases = []
+    for b, L in enumerate(lens):  # one head per sequence (heads are independent and alike)
+        c = make_case([L], [L], 1, 1, R, seed=50 + b, rel_std=0.5)
+        cases.append(tuple(t[:, 0].float().contiguous() for t in (c.q, c.k, c.v, c.rel)))
+
+    def call(i):
+        b = i % len(lens)
+        q, k, v, rel = cases[b]
+        L = lens[b]
+        return _clocked(lambda: oracle.rel_attn_rows_torch(
+            q, k, v, rel, torch.arange(L), L, L, 1.0 / D, R, True, None, "reference"),
+            4 * D * visible_pairs_causal(L))
+
+    call(0)
+    flops, used, n = _run_for(seconds, call, start=1)
+    return {"value": flops / used / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n} (sequence, head) attentions over the 16 seeded lengths (one head "
+                      "per sequence, sequences in order, repeated), dense as reference.py "
+                      "computes them; algorithmic causal FLOPs"}
+
+
+def cpu_chunked(seconds):
+    """Config 4: 128-row blocks of one sequence's 2048-token chunk (one head) against its
+    18432 keys, bottom-right alignment."""
+    import torch
+
     import oracle
     from inkling_fa4.workloads import make_case
 
-    c = make_case([SEQ], [SEQ], 1, 1, R, seed=123, rel_std=0.5)
+    threads = _cpu_threads()
+    cache, chunk = 16384, 2048
+    sk = cache + chunk
+    c = make_case([chunk], [sk], 1, 1, R, seed=60, rel_std=0.5)
     q, k, v, rel = (t[:, 0].float().contiguous() for t in (c.q, c.k, c.v, c.rel))
-    blk = 64
-    positions = [((i * 97) % (SEQ // blk)) * blk for i in range(SEQ // blk)]
 
-    def step(i):
-        r0 = positions[i % len(positions)]
-        oracle.rel_attn_rows_torch(q[r0:r0 + blk], k, v, rel[r0:r0 + blk],
-                                   torch.arange(r0, r0 + blk), SEQ, SEQ, 1.0 / D, R, True, None,
-                                   "reference")
-        return sum(4 * D * (j + 1) for j in range(r0, r0 + blk))
+    def call(i):
+        r0 = ((i * 5) % (chunk // 128)) * 128
+        return _clocked(lambda: oracle.rel_attn_rows_torch(
+            q[r0:r0 + 128], k, v, rel[r0:r0 + 128], torch.arange(r0, r0 + 128), chunk, sk,
+            1.0 / D, R, True, None, "bottom_right"),
+            sum(4 * D * (cache + r + 1) for r in range(r0, r0 + 128)))
 
+    call(0)
+    flops, used, n = _run_for(seconds, call, start=1)
+    return {"value": flops / used / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n} blocks of 128 query rows of one 2048-token chunk (one head) against "
+                      f"its {sk} keys, bottom-right alignment; algorithmic FLOPs"}
+
+
+def cpu_decode(seconds, lens):
+    """Config 5: whole sequences of the seeded decode batch (all 32 heads, one query each)
+    in a fixed order; GB/s of algorithmic bytes (K/V once per GQA group, q/rel/out).  The keys
+    of a sequence of length L are the first L of one seeded 32768-key pool."""
+    import torch
+
+    import oracle
+    from inkling_fa4.workloads import make_case
+
+    threads = _cpu_threads()
+    order = [(i * 37) % len(lens) for i in range(len(lens))]
+    pool = make_case([1], [max(lens)], HQ, HKV, R, seed=70, rel_std=0.5)
+    q, rel = pool.q.float(), pool.rel.float()
+    ks = [pool.k[:, kh].float().contiguous() for kh in range(HKV)]
+    vs = [pool.v[:, kh].float().contiguous() for kh in range(HKV)]
+    g = HQ // HKV
+    pos = torch.tensor([0])
+
+    def call(i):
+        L = lens[order[i % len(order)]]
+
+        def run():
+            for h in range(HQ):
+                oracle.rel_attn_rows_torch(q[:, h], ks[h // g][:L], vs[h // g][:L], rel[:, h],
+                                           pos, 1, L, 1.0 / D, R, True, None, "bottom_right")
+
+        return _clocked(run, L * HKV * D * 2 * 2 + HQ * (D * 2 * 2 + R * 2))
+
+    nbytes, used, n = _run_for(seconds, call)
+    gbs = nbytes / used / 1e9
+    total = sum(lens) * HKV * D * 2 * 2 + len(lens) * HQ * (D * 2 * 2 + R * 2)
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "us_per_step_extrapolated": total / (gbs * 1e9) * 1e6,
+            "sample": f"{n} whole sequences of the 128 seeded lengths (all 32 heads, one query), "
+                      "oracle port; algorithmic bytes (K/V counted once per GQA group)"}
+
+
+def run_reference_arm(args, rank, world):
+    """The reference's algorithm on the host cores, on the headline's configuration: each step
+    runs `blocks_per_step` blocks of the same CPU sample as the headline's cpu_baseline."""
+    if rank != 0:
+        return
+    threads = _cpu_threads()
+    s = CausalSample()
+    per = args.ref_blocks_per_step
     for i in range(args.warmup):
-        step(i)
+        for j in range(per):
+            s.block(i * per + j)
     flops, t0 = 0, time.perf_counter()
+    base = args.warmup * per
     for i in range(args.steps):
-        flops += step(args.warmup + i)
+        for j in range(per):
+            flops += s.block(base + i * per + j)[0]
     dt = time.perf_counter() - t0
     value = flops / dt / 1e12
-    sample = (f"per step: 1 of {HQ} heads x {blk} query rows of the 32k causal sequence, dense "
-              f"scores against all {SEQ} keys (reference.py's algorithm, oracle port, torch CPU, "
-              f"{threads} threads); algorithmic causal FLOPs")
+    sample = (f"per step: {per} blocks of the headline's CPU sample; "
+              f"{s.describe(args.steps * per)}; oracle port, torch CPU, {threads} threads")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt * 1e3 / max(1, args.steps), "higher_is_better": True,
@@ -236,6 +411,9 @@ def run_reference_arm(args, rank, world):
 
 # ---------------------------------------------------------------------------------------
 def timed(fn, steps, warmup, stream, dist=None, barrier=None):
+    """Warm up, then time `steps` calls between a barrier + synchronize on both sides with one
+    CUDA event per step on the launching stream.  Returns (total ms, median step ms), each the
+    max over ranks."""
     import torch
 
     for _ in range(warmup):
@@ -243,60 +421,83 @@ def timed(fn, steps, warmup, stream, dist=None, barrier=None):
     torch.cuda.synchronize()
     if barrier:
         barrier()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record(stream)
+    for i in range(steps):
         fn()
-    end.record(stream)
+        ev[i + 1].record(stream)
     torch.cuda.synchronize()
     if barrier:
         barrier()
-    ms = start.elapsed_time(end)
+    ms = ev[0].elapsed_time(ev[-1])
+    med = statistics.median(ev[i].elapsed_time(ev[i + 1]) for i in range(steps))
     if dist is not None:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        t = torch.tensor([ms, med], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return ms
+        ms, med = float(t[0].item()), float(t[1].item())
+    return ms, med
+
+
+def read_stream_peak(dev):
+    """A read-only HBM stream on this GPU, measured in the run: torch's sum over a 4 GiB bf16
+    buffer (best of 10, CUDA events).  Decode reads ~99 % and writes ~1 % of its bytes, so its
+    natural ceiling is a read stream, which runs faster than the read+write copy of
+    MEASURED_PEAKS.json."""
+    import torch
+
+    x = torch.ones(1 << 31, dtype=torch.bfloat16, device=dev)
+    best = float("inf")
+    for i in range(13):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        x.sum()
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            best = min(best, a.elapsed_time(b))
+    gbs = x.numel() * 2 / (best / 1e3) / 1e9
+    del x
+    torch.cuda.empty_cache()
+    return gbs
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds", type=float, default=6.0,
+                    help="CPU work per configuration's cpu_baseline sample")
+    ap.add_argument("--ref-blocks-per-step", type=int, default=8,
+                    help="reference arm: 128-row blocks of the CPU sample per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--no-window", action="store_true")
-    ap.add_argument("--no-backward", action="store_true")
-    ap.add_argument("--no-rel-logits", action="store_true")
+    ap.add_argument("--skip", default="", help=f"comma-separated legs to skip, of {LEGS}")
+    ap.add_argument("--only", default="all",
+                    help="'headline', or one leg name (profiling runs); 'all' runs everything")
     ap.add_argument("--no-shard", action="store_true",
-                    help="skip the head-sharded single-sequence leg (N > 1 only)")
-    ap.add_argument("--extra-configs", action="store_true",
-                    help="also time BASELINE configs 2 (ragged) and 4 (chunked)")
-    ap.add_argument("--only", choices=["all", "prefill", "decode", "rel_logits"], default="all",
-                    help="prefill: headline + window only; decode: decode only; rel_logits: the "
-                         "producer only (profiling runs)")
+                    help="skip the head-sharded legs (N > 1 only)")
     ap.add_argument("--prefill-seq", type=int, default=SEQ,
-                    help="sequence length of the prefill workload (32768 = BASELINE config 3)")
+                    help="sequence length of the headline workload (32768 = BASELINE config 3)")
     ap.add_argument("--tile-config", type=int, default=0,
                     help="prefill kernel variant (0 = default; see autotune_configs)")
     ap.add_argument("--decode-batch", type=int, default=128,
                     help="decode batch (128 = BASELINE config 5)")
     args = ap.parse_args()
-    if args.only == "prefill":
-        args.no_decode = args.no_rel_logits = args.no_shard = True
-    if args.only == "decode":
-        args.no_e2e = args.no_window = args.no_backward = args.no_rel_logits = True
-        args.no_shard = True
-    if args.only == "rel_logits":
-        args.no_e2e = args.no_window = args.no_backward = args.no_decode = True
-        args.no_shard = True
     if args.warmup < 3:
         args.warmup = 3
+    skip = {s for s in args.skip.split(",") if s}
+    bad = skip - set(LEGS)
+    if bad:
+        ap.error(f"unknown legs {sorted(bad)}")
+    if args.only != "all":
+        if args.only != "headline" and args.only not in LEGS:
+            ap.error(f"--only must be 'all', 'headline' or one of {LEGS}")
+        skip = set(LEGS) - {args.only}
+        args.no_shard = True
+        args.no_cpu_baseline = True
+    want = lambda leg: leg not in skip
+    run_headline = args.only in ("all", "headline", "e2e")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -326,30 +527,49 @@ def main():
         dist = tdist
     barrier = (lambda: dist.barrier()) if dist else None
 
-    from inkling_fa4 import (_lib, inkling_fa4_rel_attention_decode_triton,
+    from inkling_fa4 import (_lib, _ops, inkling_fa4_rel_attention_decode_triton,
                              inkling_fa4_rel_attention_triton)
-    from inkling_fa4.workloads import config_decode, config_long
+    from inkling_fa4.workloads import (causal_visible_pairs, config_chunked, config_decode,
+                                       config_long, config_ragged, make_case, page_kv)
 
     peaks, peak_kind = load_peaks()
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(dev)
-
-    # ---------------- headline: 32k causal prefill, inputs resident in HBM
-    S = args.prefill_seq
-    c = config_long(device=dev, seed=rank, seq=S, gen_device=dev)
-    flops = 4 * D * HQ * visible_pairs_causal(S)
-
-    from inkling_fa4 import _ops
+    steps2, warm2 = max(args.steps, 50), max(args.warmup, 10)  # secondary legs
+    cpu_on = rank == 0 and world == 1 and not args.no_cpu_baseline
 
     def prefill_call(*pa, **kw):
         """The public prefill entry point, or the same call pinned to --tile-config (for tile
-        sweeps; applies to the headline, window, ragged and chunked legs)."""
-        if args.tile_config:
+        sweeps; paged caches exist for tile configs 0 to 3)."""
+        if args.tile_config and (kw.get("block_table") is None or args.tile_config <= 3):
             return _ops.prefill(*pa, tile_config=args.tile_config, **kw)
         return inkling_fa4_rel_attention_triton(*pa, **kw)
 
-    def prefill_step():
-        return prefill_call(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R)
+    def tensor_roofline(flops_per_step, ms_step, traffic=None, kernel="rel_attn_prefill_kernel"):
+        achieved = flops_per_step / (ms_step / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "peak_source": f"bf16_tflops (burst) of {peak_kind}",
+                "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
+                "frac_of_datasheet_2250": achieved / DATASHEET["bf16_tflops"],
+                "traffic": traffic, "kernel": f"{kernel} (1 launch per step)"}
+
+    def prefill_leg(name, case, flops, steps, warmup, extra_cfg, **kw):
+        def step():
+            return prefill_call(case.q, case.k, case.v, case.rel, case.cu_q, case.cu_k,
+                                case.max_q, case.max_k, case.rel_extent, **kw)
+
+        ms, med = timed(step, steps, warmup, stream, dist, barrier)
+        ms_step = ms / steps
+        cfg = {"rel_extent": case.rel_extent, "batch": len(case.seqlens_q),
+               "total_q": int(case.q.shape[0]), "total_k": int(case.cu_k[-1].item()),
+               "n_heads": int(case.q.shape[1]),
+               "kv_heads": int(case.k.shape[-2]), "flops_per_step_per_gpu": flops}
+        cfg.update(extra_cfg)
+        return {"value": world * flops * steps / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": ms_step, "ms_per_step_median": med, "steps": steps,
+                "warmup": warmup, "config": cfg,
+                "roofline": tensor_roofline(flops, med), "gpu_launches": steps}
 
     uuids = []
     try:
@@ -357,21 +577,29 @@ def main():
     except Exception:
         pass
     sampler = ClockSampler(uuids) if rank == 0 else None
-    if args.only in ("decode", "rel_logits"):
-        ms, clocks = float("nan"), None
+    if sampler:
+        sampler.start()
+
+    # ---------------- headline: 32k causal prefill, inputs resident in HBM
+    S = args.prefill_seq
+    c = config_long(device=dev, seed=rank, seq=S, gen_device=dev)
+    flops = 4 * D * HQ * visible_pairs_causal(S)
+
+    def prefill_step():
+        return prefill_call(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R)
+
+    if run_headline:
+        ms, med = timed(prefill_step, args.steps, args.warmup, stream, dist, barrier)
     else:
-        if sampler:
-            sampler.start()
-        ms = timed(prefill_step, args.steps, args.warmup, stream, dist, barrier)
-        clocks = sampler.stop() if sampler else None
+        ms, med = float("nan"), float("nan")
     ms_step = ms / args.steps
     value = world * flops * args.steps / (ms / 1e3) / 1e12
-    achieved = flops / (ms_step / 1e3) / 1e12
     status = _lib.read_device_status(stream.cuda_stream)
 
     result = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "ms_per_step_median": med,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) q/k/v and N(0,0.5) per-token rel logits, generated on "
                 "the device (rank r uses seed r)",
@@ -383,28 +611,22 @@ def main():
                    "l2": (f"no flush; inputs of {(S * (HQ * (2 * D + 2 * R) + HKV * 4 * D)) >> 20} MB "
                           "per step exceed the 126 MB L2"),
                    "parallelism": f"{world} independent {S}-token sequences, one per rank (weak)"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "peak_source": f"bf16_tflops (burst) of {peak_kind}",
-                     "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
-                     "frac_of_datasheet_2250": achieved / 2250.0,
-                     "traffic": profile_traffic("prefill_dram_traffic.md") if S == SEQ else None,
-                     "traffic_note": "one-pass ncu capture of the 32k launch "
-                                     "(profiles/prefill_dram_traffic.md)",
-                     "kernel": "rel_attn_prefill_kernel (1 launch per step)",
-                     "tile_config": args.tile_config},
-        "gpu_launches": args.steps,
+        "roofline": dict(tensor_roofline(flops, ms_step,
+                                         NCU_DRAM_BYTES_PER_LAUNCH["prefill_causal32k"]
+                                         if S == SEQ else None),
+                         traffic_note="ncu one-pass capture of the full-size 32k launch "
+                                      "(dram__bytes_read.sum + dram__bytes_write.sum)",
+                         tile_config=args.tile_config),
+        "gpu_launches": args.steps if run_headline else 0,
         "device_status": status,
     }
-    if clocks:
-        result["clocks"] = clocks
 
     # ---------------- end to end through the public API with host buffers
     # Every step uploads its own inputs from pinned host memory, runs the public API call and
     # downloads its output to pinned host memory.  Three streams and two buffer sets let the
     # upload of step i+1 and the download of step i-1 overlap the kernel of step i, as a
     # serving pipeline would; the timed region spans the first upload to the last download.
-    if not args.no_e2e:
+    if run_headline and want("e2e"):
         names = ("q", "k", "v", "rel", "cu_q", "cu_k")
         host = {n: getattr(c, n).cpu().pin_memory() for n in names}
         dbuf = [{n: torch.empty_like(getattr(c, n)) for n in names} for _ in range(2)]
@@ -469,21 +691,15 @@ def main():
                                  "moves its own inputs and output"}
         del host, dbuf, dout, hout
 
-    # ---------------- sliding window 4096 at 32k (BASELINE config 3b)
-    if not args.no_window:
+    # ---------------- config 3b: sliding window 4096 at 32k
+    if want("window"):
         wflops = 4 * D * HQ * visible_pairs_causal(S, 4096)
-
-        def win_step():
-            return prefill_call(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S, R,
-                                window_size=(4096, 0))
-
-        wms = timed(win_step, args.steps, args.warmup, stream, dist, barrier)
-        result["window32k"] = {"value": world * wflops * args.steps / (wms / 1e3) / 1e12,
-                               "unit": "TFLOP/s", "ms_per_step": wms / args.steps,
-                               "window_left": 4096, "flops_per_step_per_gpu": wflops}
+        result["window32k"] = prefill_leg("window32k", c, wflops, steps2, warm2,
+                                          {"workload": "window4096_32k_gqa32_8_d128_rel128",
+                                           "window_left": 4096}, window_size=(4096, 0))
 
     # ---------------- backward of the headline prefill (not in the reference)
-    if not args.no_backward:
+    if want("backward"):
         from inkling_fa4 import inkling_fa4_rel_attention_backward
 
         bout, blse = inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S,
@@ -500,22 +716,23 @@ def main():
                 bdout, c.q, c.k, c.v, c.rel, bout, blse, c.cu_q, c.cu_k, S, S, R, dq=bufs[0],
                 dk=bufs[1], dv=bufs[2], drel=bufs[3], workspace=bws)
 
-        bsteps = max(5, args.steps // 5)
-        bms = timed(bwd_step, bsteps, args.warmup, stream, dist, barrier)
+        bsteps = max(5, args.steps // 2)
+        bms, bmed = timed(bwd_step, bsteps, args.warmup, stream, dist, barrier)
         bflops = 2.5 * flops  # 5 matrix products of the forward's size (the usual convention)
         result["backward32k"] = {
             "value": world * bflops * bsteps / (bms / 1e3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": bms / bsteps, "steps": bsteps,
+            "ms_per_step": bms / bsteps, "ms_per_step_median": bmed, "steps": bsteps,
             "flops_per_step_per_gpu": bflops,
             "flops_note": "algorithmic 2.5x forward (S, dP, dV, dK, dQ); the kernels execute "
                           "3.5x (S and dP are recomputed by the dQ kernel to avoid atomics)",
-            "kernels": "rel_attn_bwd_prep_kernel, rel_attn_bwd_dkdv_kernel, "
-                       "rel_attn_bwd_dq_kernel (3 launches per step)",
+            "roofline": dict(tensor_roofline(bflops, bmed), kernel="rel_attn_bwd_prep_kernel, "
+                             "rel_attn_bwd_dkdv_kernel, rel_attn_bwd_dq_kernel (3 launches per "
+                             "step; algorithmic FLOPs over the whole step)"),
             "gpu_launches": 3 * bsteps}
         del bout, blse, bdout, bws, bufs
 
     # ---------------- rel_logits producer for the headline shape (the step before the path)
-    if not args.no_rel_logits:
+    if want("rel_logits"):
         from inkling_fa4 import inkling_rel_logits
 
         gen = torch.Generator(device=dev)
@@ -527,17 +744,17 @@ def main():
         def rl_step():
             return inkling_rel_logits(rr, rw, alpha=0.1, nf=4096.0, out=rout)
 
-        rms = timed(rl_step, args.steps, args.warmup, stream, dist, barrier)
+        rms, rmed = timed(rl_step, steps2, warm2, stream, dist, barrier)
         rbytes = rr.numel() * 2 + rw.numel() * 2 + rout.numel() * 2
-        rgbs = rbytes * args.steps / (rms / 1e3) / 1e9
+        rgbs = rbytes * steps2 / (rms / 1e3) / 1e9
         # Write-stream reference on the same box: torch's fill_ of the same output buffer, same
-        # protocol (the producer's traffic is 89 % writes; a plain write stream reaches well
-        # below the read+write copy peak).
-        fms = timed(lambda: rout.fill_(1.0), args.steps, args.warmup, stream, dist, barrier)
-        fill_gbs = rout.numel() * 2 * args.steps / (fms / 1e3) / 1e9
-        write_gbs = rout.numel() * 2 * args.steps / (rms / 1e3) / 1e9
+        # protocol (the producer's traffic is 89 % writes).
+        fms, _ = timed(lambda: rout.fill_(1.0), steps2, warm2, stream, dist, barrier)
+        fill_gbs = rout.numel() * 2 * steps2 / (fms / 1e3) / 1e9
+        write_gbs = rout.numel() * 2 * steps2 / (rms / 1e3) / 1e9
         result["rel_logits32k"] = {
-            "value": world * rgbs, "unit": "GB/s", "us_per_step": rms * 1e3 / args.steps,
+            "value": world * rgbs, "unit": "GB/s", "us_per_step": rms * 1e3 / steps2,
+            "us_per_step_median": rmed * 1e3, "steps": steps2,
             "config": {"workload": "rel_logits_32k_h32_r128", "tokens": S, "n_heads": HQ,
                        "d_rel": 16, "rel_extent": R, "weight": "per head", "alpha": 0.1,
                        "nf": 4096.0, "bytes_per_step_per_gpu": rbytes,
@@ -548,89 +765,172 @@ def main():
                          "peak_source": f"hbm_gbs of {peak_kind}",
                          "write_gbs": write_gbs, "fill_gbs_same_buffer": fill_gbs,
                          "write_frac_of_fill": write_gbs / fill_gbs,
-                         "traffic": (profile_traffic("rel_logits_32k_ncu.md")
+                         "traffic": (NCU_DRAM_BYTES_PER_LAUNCH["rel_logits32k"]
                                      if S == SEQ else None),
                          "traffic_note": "one cold ncu launch: reads + writes performed before "
                                          "it ended (54 MB of output still dirty in L2)"},
-            "kernel": "rel_logits_kernel (1 launch per step)", "gpu_launches": args.steps}
+            "kernel": "rel_logits_kernel (1 launch per step)", "gpu_launches": steps2}
         del rr, rw, rout
     del c
     torch.cuda.empty_cache()
 
-    # ---------------- one 32k sequence sharded by KV-head group over the ranks (N > 1 only)
-    # Strong scaling of a single call: rank r runs the heads of kv groups [r*8/N, (r+1)*8/N) of
-    # the same sequence (head-slice views, no copies), timed without and with the NCCL
-    # all-gather that assembles the [T, 32, 128] output on every rank.
+    # ---------------- config 2: ragged 16 x U[1, 4096], config 4: chunked 8 x (16384 + 2048)
+    for name, make, align in (("ragged", config_ragged, "reference"),
+                              ("chunked", config_chunked, "bottom_right")):
+        if not want(name):
+            continue
+        cc = make(device=dev, seed=rank, gen_device=dev)
+        fl = 4 * D * HQ * causal_visible_pairs(cc.seqlens_q, cc.seqlens_k, causal_align=align)
+        cfg = {"workload": cc.meta["name"], "causal_align": align}
+        if name == "ragged":
+            cfg["seqlens"] = cc.seqlens_q
+        result[name] = prefill_leg(name, cc, fl, steps2, warm2, cfg, causal_align=align)
+        if name == "chunked":  # the same chunks against a 16-token paged cache
+            pc = page_kv(cc, page_size=16, seed=rank)
+            del cc
+            cc = pc
+            leg = prefill_leg("chunked_paged", pc, fl, steps2, warm2,
+                              dict(cfg, page_size=16, num_pages=pc.meta["num_pages"]),
+                              causal_align=align, block_table=pc.meta["block_table"])
+            result["chunked_paged"] = leg
+        del cc
+        torch.cuda.empty_cache()
+
+    # ---------------- the rel extents the model and the reference's benchmark use
+    # Global layers: R = 1024, full causal; local layers: R = 512 with window (511, 0)
+    # (the reference's architecture notes); the reference's benchmark: S = 4096, Hq = Hkv = 4,
+    # R = 1024, causal (its only published numbers).
+    for name, seq, hq, hkv, rext, win in (("global_rel1024", S, HQ, HKV, 1024, None),
+                                          ("local_rel512", S, HQ, HKV, 512, 511),
+                                          ("refbench", 4096, 4, 4, 1024, None)):
+        if not want(name):
+            continue
+        gc = make_case([seq], [seq], hq, hkv, rext, seed=rank, device=dev, rel_std=0.5,
+                       gen_device=dev)
+        fl = 4 * D * hq * visible_pairs_causal(seq, win)
+        kw = {} if win is None else {"window_size": (win, 0)}
+        key = {"global_rel1024": f"global{seq}_rel1024", "local_rel512": f"local{seq}_rel512_window511",
+               "refbench": "refbench4096_h4_rel1024"}[name]
+        leg = prefill_leg(key, gc, fl, steps2, warm2,
+                          {"workload": f"{key}_gqa{hq}_{hkv}_d128", "seq_len": seq,
+                           "window_left": win}, **kw)
+        if name == "refbench":
+            leg["reference_published_ms_rtx3090"] = REF_PUBLISHED_MS_S4096
+            leg["speedup_vs_published"] = REF_PUBLISHED_MS_S4096 / leg["ms_per_step_median"]
+        result[key] = leg
+        del gc
+        torch.cuda.empty_cache()
+
+    # ---------------- config 1 on the GPU (bf16 inputs; the configuration is the CPU case)
+    if want("config1"):
+        from inkling_fa4.workloads import config_cpu_reference
+
+        c1 = config_cpu_reference(device=dev)
+        fl1 = 4 * D * 4 * visible_pairs_causal(128)
+        leg = prefill_leg("config1", c1, fl1, steps2, warm2,
+                          {"workload": "cpu_reference_s128_h4_4_rel128_table",
+                           "softmax_scale": 128 ** -0.5, "rel": "per-head table (token stride 0)",
+                           "note": "launch-latency bound: one 128-row tile per head"},
+                          softmax_scale=128 ** -0.5)
+        result["config1"] = leg
+        del c1
+
+    # ---------------- one problem split over the ranks by KV-head group (N > 1 only)
+    # Strong scaling of a single call: rank r runs the heads of kv groups [r*8/N, (r+1)*8/N)
+    # (head-slice views, no copies), timed without and with the NCCL all-gather that assembles
+    # the full output on every rank, and checked against the rank's own unsharded call on the
+    # same inputs (the per-head arithmetic is identical, so the outputs are equal bit for bit).
     if world > 1 and not args.no_shard and HKV % world == 0:
         from inkling_fa4.sharding import gather_heads, head_shard, shard_tensors
 
-        sc = config_long(device=dev, seed=0, seq=S, gen_device=dev)  # same sequence on all ranks
         sh = head_shard(HQ, HKV, world, rank)
+        sc = config_long(device=dev, seed=0, seq=S, gen_device=dev)  # same sequence on all ranks
         q_s, k_s, v_s, rel_s = shard_tensors(sh, sc.q, sc.k, sc.v, sc.rel)
         shard_step = lambda: inkling_fa4_rel_attention_triton(q_s, k_s, v_s, rel_s, sc.cu_q,
                                                                sc.cu_k, S, S, R)
         gather_step = lambda: gather_heads(shard_step(), world)
-        ms_ng = timed(shard_step, args.steps, args.warmup, stream, dist, barrier)
-        ms_g = timed(gather_step, args.steps, args.warmup, stream, dist, barrier)
+        ms_ng, _ = timed(shard_step, args.steps, args.warmup, stream, dist, barrier)
+        ms_g, _ = timed(gather_step, args.steps, args.warmup, stream, dist, barrier)
+        full = gather_step()
+        ref = inkling_fa4_rel_attention_triton(sc.q, sc.k, sc.v, sc.rel, sc.cu_q, sc.cu_k, S, S,
+                                               R)
+        diff = float((full.float() - ref.float()).abs().max().item())
+        ok = torch.tensor([1 if torch.equal(full, ref) else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         full_flops = 4 * D * HQ * visible_pairs_causal(S)
+        # NCCL's own time for the 32 MB-per-rank all-gather alone (the output of this rank)
+        src = torch.empty((S, sh.n_q, D), dtype=torch.bfloat16, device=dev)
+        gbuf = torch.empty((world, S, sh.n_q, D), dtype=torch.bfloat16, device=dev)
+        ag_ms, _ = timed(lambda: dist.all_gather_into_tensor(gbuf, src), args.steps, args.warmup,
+                         stream, dist, barrier)
+        ag_bytes = gbuf.numel() * 2
         result["head_sharded32k"] = {
             "unit": "TFLOP/s", "scaling": "strong",
             "value_no_gather": full_flops * args.steps / (ms_ng / 1e3) / 1e12,
             "value_with_gather": full_flops * args.steps / (ms_g / 1e3) / 1e12,
             "ms_per_step_no_gather": ms_ng / args.steps,
             "ms_per_step_with_gather": ms_g / args.steps,
+            "parity_ok": bool(ok.item() == 1), "max_abs_diff_vs_unsharded": diff,
+            "nccl_all_gather_alone": {"ms": ag_ms / args.steps,
+                                      "bus_gbs": ag_bytes * (world - 1) / world
+                                      / (ag_ms / args.steps / 1e3) / 1e9,
+                                      "bytes_per_rank": src.numel() * 2},
             "config": {"workload": "causal32k_gqa32_8_d128_rel128, one sequence",
                        "heads_per_rank": sh.n_q, "kv_heads_per_rank": sh.n_kv,
                        "collective": "one NCCL all_gather_into_tensor of the output heads "
                                      f"({S * HQ * D * 2 >> 20} MB assembled per step)"},
             "gpu_launches": args.steps}
-        del sc, q_s, k_s, v_s, rel_s
+        del sc, q_s, k_s, v_s, rel_s, full, ref, src, gbuf
         torch.cuda.empty_cache()
 
-    # ---------------- ragged (config 2) and chunked (config 4) prefill, on request
-    if args.extra_configs:
-        from inkling_fa4.workloads import (causal_visible_pairs, config_chunked, config_ragged,
-                                           page_kv)
+        # config 5 decode with its KV heads split 8/N per rank (same batch on every rank)
+        dcs = config_decode(device=dev, seed=0, batch=args.decode_batch, gen_device=dev)
+        lens = dcs.seqlens_k
+        p = _ops._decode_params(dcs.q, dcs.k, dcs.v, dcs.rel, dcs.q, dcs.cu_q, dcs.cu_k, HQ, HKV,
+                                R, True, -1, "bottom_right", max(lens), 1.0 / D, 0, 0)
+        _, nsplit, chunk = _ops.decode_plan(p)
+        dq, dk, dv, drel = shard_tensors(sh, dcs.q, dcs.k, dcs.v, dcs.rel)
+        ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
 
-        for name, make, align in (("ragged", config_ragged, "reference"),
-                                  ("chunked", config_chunked, "bottom_right")):
-            cc = make(device=dev, seed=rank, gen_device=dev)
-            fl = 4 * D * HQ * causal_visible_pairs(cc.seqlens_q, cc.seqlens_k,
-                                                   causal_align=align)
+        def dshard_step():
+            return inkling_fa4_rel_attention_decode_triton(
+                dq, dk, dv, drel, dcs.cu_q, dcs.cu_k, 1, max(lens), R, causal_align="bottom_right",
+                num_splits=nsplit, chunk_len=chunk, workspace=ws)
 
-            def step(cc=cc, align=align):
-                return prefill_call(cc.q, cc.k, cc.v, cc.rel, cc.cu_q, cc.cu_k, cc.max_q,
-                                    cc.max_k, R, causal_align=align)
-
-            xms = timed(step, args.steps, args.warmup, stream, dist, barrier)
-            result[name] = {"value": world * fl * args.steps / (xms / 1e3) / 1e12,
-                            "unit": "TFLOP/s", "ms_per_step": xms / args.steps,
-                            "flops_per_step_per_gpu": fl, "causal_align": align,
-                            "seqlens_q": cc.seqlens_q if name == "ragged" else None}
-            if name == "chunked":  # the same chunks against a 16-token paged cache
-                pc = page_kv(cc, page_size=16, seed=rank)
-                del cc
-
-                # paged caches exist for tile configs 0 to 3; other sweep values run the default
-                paged_call = prefill_call if args.tile_config <= 3 else \
-                    inkling_fa4_rel_attention_triton
-
-                def pstep(pc=pc):
-                    return paged_call(
-                        pc.q, pc.k, pc.v, pc.rel, pc.cu_q, pc.cu_k, pc.max_q, pc.max_k, R,
-                        causal_align="bottom_right", block_table=pc.meta["block_table"])
-
-                pms = timed(pstep, args.steps, args.warmup, stream, dist, barrier)
-                result["chunked_paged"] = {
-                    "value": world * fl * args.steps / (pms / 1e3) / 1e12, "unit": "TFLOP/s",
-                    "ms_per_step": pms / args.steps, "flops_per_step_per_gpu": fl,
-                    "page_size": 16, "num_pages": pc.meta["num_pages"]}
-                cc = pc
-            del cc
+        dgather_step = lambda: gather_heads(dshard_step(), world)
+        dms_ng, dmed_ng = timed(dshard_step, steps2, warm2, stream, dist, barrier)
+        dms_g, _ = timed(dgather_step, steps2, warm2, stream, dist, barrier)
+        dfull = dgather_step()
+        dref = inkling_fa4_rel_attention_decode_triton(
+            dcs.q, dcs.k, dcs.v, dcs.rel, dcs.cu_q, dcs.cu_k, 1, max(lens), R,
+            causal_align="bottom_right", num_splits=nsplit, chunk_len=chunk, workspace=ws)
+        ddiff = float((dfull.float() - dref.float()).abs().max().item())
+        dok = torch.tensor([1 if torch.equal(dfull, dref) else 0], device=dev)
+        dist.all_reduce(dok, op=dist.ReduceOp.MIN)
+        total_bytes = sum(lens) * HKV * D * 2 * 2 + len(lens) * HQ * (D * 2 * 2 + R * 2)
+        rank_bytes = total_bytes // world
+        rank_gbs = rank_bytes / (dmed_ng / 1e3) / 1e9
+        result["decode_head_sharded"] = {
+            "unit": "GB/s", "scaling": "strong",
+            "value_no_gather": total_bytes * steps2 / (dms_ng / 1e3) / 1e9,
+            "value_with_gather": total_bytes * steps2 / (dms_g / 1e3) / 1e9,
+            "us_per_step_no_gather": dms_ng * 1e3 / steps2,
+            "us_per_step_with_gather": dms_g * 1e3 / steps2,
+            "per_rank_gbs": rank_gbs, "per_rank_frac_of_hbm": rank_gbs / peaks["hbm_gbs"],
+            "parity_ok": bool(dok.item() == 1), "max_abs_diff_vs_unsharded": ddiff,
+            "config": {"workload": "decode128_u1024_32768_gqa32_8_d128_rel128",
+                       "kv_heads_per_rank": sh.n_kv, "heads_per_rank": sh.n_q,
+                       "num_splits": nsplit, "chunk_len": chunk,
+                       "bytes_per_step_total": total_bytes,
+                       "collective": "one NCCL all_gather_into_tensor of the output heads "
+                                     f"({len(lens) * HQ * D * 2 >> 10} KB assembled per step)"},
+            "gpu_launches": steps2 * (2 if nsplit > 1 else 1)}
+        del dcs, dq, dk, dv, drel, ws, dfull, dref
         torch.cuda.empty_cache()
 
-    # ---------------- batched decode
-    if not args.no_decode:
+    # ---------------- config 5: batched decode (contiguous and paged)
+    if want("decode"):
+        read_gbs = read_stream_peak(dev)
         dc = config_decode(device=dev, seed=rank, batch=args.decode_batch, gen_device=dev)
         lens = dc.seqlens_k
         kv_bytes = sum(lens) * HKV * D * 2 * 2
@@ -643,28 +943,60 @@ def main():
                 dc.q, dc.k, dc.v, dc.rel, dc.cu_q, dc.cu_k, 1, max(lens), R,
                 causal_align="bottom_right", workspace=ws)
 
-        from inkling_fa4 import _ops
         p = _ops._decode_params(dc.q, dc.k, dc.v, dc.rel, dc.q, dc.cu_q, dc.cu_k, HQ, HKV, R,
                                 True, -1, "bottom_right", max(lens), 1.0 / D, 0, 0)
         _, nsplit, chunk = _ops.decode_plan(p)
-        dms = timed(dec_step, args.steps, args.warmup, stream, dist, barrier)
-        us = dms * 1e3 / args.steps
-        gbs = world * dbytes * args.steps / (dms / 1e3) / 1e9
-        per_gpu = dbytes / (us / 1e6) / 1e9
+        dms, dmed = timed(dec_step, steps2, warm2, stream, dist, barrier)
+        us = dms * 1e3 / steps2
+        gbs = world * dbytes * steps2 / (dms / 1e3) / 1e9
+        per_gpu = dbytes / (dmed / 1e3) / 1e9
+
+        def hbm_roofline(achieved):
+            return {"bound": "hbm", "achieved": achieved, "peak": read_gbs, "unit": "GB/s",
+                    "frac": achieved / read_gbs,
+                    "peak_source": "read-only stream measured in this run (torch sum over a "
+                                   "4 GiB bf16 buffer, best of 10)",
+                    "frac_of_copy_peak": achieved / peaks["hbm_gbs"],
+                    "copy_peak": peaks["hbm_gbs"],
+                    "copy_peak_source": f"hbm_gbs (read+write copy) of {peak_kind}",
+                    "frac_of_datasheet_7700": achieved / DATASHEET["hbm_gbs"]}
+
+        # host-side cost of one call at small batch: wall clock around the Python call
+        # (argument checks, ctypes, workspace planning) against the device time of the same call
+        small = config_decode(device=dev, seed=rank, batch=1, gen_device=dev)
+        sws = torch.empty(8 << 20, dtype=torch.uint8, device=dev)
+        small_step = lambda: inkling_fa4_rel_attention_decode_triton(
+            small.q, small.k, small.v, small.rel, small.cu_q, small.cu_k, 1, small.max_k, R,
+            causal_align="bottom_right", workspace=sws)
+        for _ in range(20):
+            small_step()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(200):
+            small_step()
+        host_us = (time.perf_counter() - t0) / 200 * 1e6
+        torch.cuda.synchronize()
+        sms, smed = timed(small_step, steps2, warm2, stream)
         result["decode"] = {
-            "value": gbs, "unit": "GB/s", "us_per_step": us,
+            "value": gbs, "unit": "GB/s", "us_per_step": us, "us_per_step_median": dmed * 1e3,
+            "steps": steps2,
             "config": {"workload": "decode128_u1024_32768_gqa32_8_d128_rel128",
                        "batch": len(lens), "kv_tokens": sum(lens),
                        "causal_align": "bottom_right", "num_splits": nsplit, "chunk_len": chunk,
                        "bytes_per_step_per_gpu": dbytes},
-            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peaks["hbm_gbs"],
-                         "unit": "GB/s", "frac": per_gpu / peaks["hbm_gbs"],
-                         "peak_source": f"hbm_gbs of {peak_kind}",
-                         "traffic": (profile_traffic("decode_dram_traffic.md")
-                                     if args.decode_batch == 128 else None)},
-            "gpu_launches": args.steps * (2 if nsplit > 1 else 1)}
+            "roofline": dict(hbm_roofline(per_gpu),
+                             traffic=(NCU_DRAM_BYTES_PER_LAUNCH["decode128"]
+                                      if args.decode_batch == 128 else None),
+                             traffic_note="batch-16 ncu capture scaled to batch 128 by K/V bytes"),
+            "host_call_overhead_b1": {
+                "host_us_per_call": host_us, "device_us_per_call_median": smed * 1e3,
+                "kv_tokens": small.max_k,
+                "note": "wall clock of 200 back-to-back Python calls (argument checks, ctypes "
+                        "struct, plan query, 2 launches) vs CUDA-event device time; the host "
+                        "cost hides behind the device when it is the smaller"},
+            "gpu_launches": steps2 * (2 if nsplit > 1 else 1)}
+        del small, sws
         # the same step against a 16-token paged cache (pages handed out in random order)
-        from inkling_fa4.workloads import page_kv
         pdc = page_kv(dc, page_size=16, seed=rank)
         del dc
         torch.cuda.empty_cache()
@@ -674,24 +1006,41 @@ def main():
                 pdc.q, pdc.k, pdc.v, pdc.rel, pdc.cu_q, pdc.cu_k, 1, max(lens), R,
                 causal_align="bottom_right", workspace=ws, block_table=pdc.meta["block_table"])
 
-        pms = timed(paged_step, args.steps, args.warmup, stream, dist, barrier)
-        pus = pms * 1e3 / args.steps
+        pms, pmed = timed(paged_step, steps2, warm2, stream, dist, barrier)
+        pbytes = dbytes + 4 * sum((n + 15) // 16 for n in lens)
         result["decode_paged"] = {
-            "value": world * dbytes * args.steps / (pms / 1e3) / 1e9, "unit": "GB/s",
-            "us_per_step": pus, "page_size": 16, "num_pages": pdc.meta["num_pages"],
-            "frac": dbytes / (pus / 1e6) / 1e9 / peaks["hbm_gbs"],
-            "bytes_per_step_per_gpu": dbytes + 4 * sum((n + 15) // 16 for n in lens)}
-        dc = pdc
-        del dc, ws
+            "value": world * pbytes * steps2 / (pms / 1e3) / 1e9, "unit": "GB/s",
+            "us_per_step": pms * 1e3 / steps2, "us_per_step_median": pmed * 1e3,
+            "page_size": 16, "num_pages": pdc.meta["num_pages"],
+            "bytes_per_step_per_gpu": pbytes,
+            "roofline": hbm_roofline(pbytes / (pmed / 1e3) / 1e9),
+            "gpu_launches": steps2 * (2 if nsplit > 1 else 1)}
+        del pdc, ws
         torch.cuda.empty_cache()
 
     result["device_status"] = _lib.read_device_status(stream.cuda_stream)
+    clocks = sampler.stop() if sampler else None
+    if clocks:
+        result["clocks"] = clocks
 
-    # ---------------- CPU baseline (rank 0, N = 1)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only == "all":
-        v, cores, sample = cpu_baseline_prefill(args.cpu_seconds)
-        result["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                                  "sample": sample}
+    # ---------------- CPU baselines (rank 0, N = 1): the oracle port on bounded samples
+    if cpu_on:
+        from inkling_fa4.workloads import decode_batch_lengths
+
+        secs = args.cpu_seconds
+        if run_headline:
+            result["cpu_baseline"] = cpu_causal32k(secs)
+        if "window32k" in result:
+            result["window32k"]["cpu_baseline"] = cpu_causal32k(secs / 2, window=4096)
+        if "ragged" in result:
+            result["ragged"]["cpu_baseline"] = cpu_ragged(secs)
+        if "chunked" in result:
+            result["chunked"]["cpu_baseline"] = cpu_chunked(secs)
+        if "config1" in result:
+            result["config1"]["cpu_baseline"] = cpu_config1(secs / 3)
+        if "decode" in result:
+            result["decode"]["cpu_baseline"] = cpu_decode(
+                secs, decode_batch_lengths(batch=args.decode_batch))
 
     if dist is not None:
         dist.barrier()

@@ -8,6 +8,12 @@
  * Every entry point returns 0 on success or a negative IFA4_ERR_* code; the message of the
  * last failure on the calling thread is available from ifa4_last_error_string().
  *
+ * Lifetime: the library caches, per device, the device addresses of its own __device__
+ * objects (the status word, the no-allocation decode scratch).  Those addresses belong to the
+ * device's primary context, so the library must not be used across a cudaDeviceReset() (or
+ * any other destruction of the primary context) in the same process: the cached addresses
+ * would then point into a released context.
+ *
  * Semantics follow the reference oracle ref_rel_attn (src/inkling_fa4/reference.py:4-39 of
  * KINGXD414/Inkling-FA4-Relative-Attention): scores = (q k^T) * scale; bias
  * rel[q, h, d] with d = q_pos + bias_shift - k_pos applied only when 0 <= d < rel_extent;

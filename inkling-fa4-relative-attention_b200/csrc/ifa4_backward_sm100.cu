@@ -930,31 +930,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace bwd
 
-namespace {
-template <class K>
-cudaError_t set_smem(K kernel, uint32_t bytes, bool* done) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!done[dev]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(bytes));
-    if (e != cudaSuccess) return e;
-    done[dev] = true;
-  }
-  return cudaSuccess;
-}
-}  // namespace
-
 cudaError_t launch_backward_sm100(const BackwardKernelArgs& args, const CUtensorMap& tm_q,
                                   const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                   const CUtensorMap& tm_do, int q_slots, int k_slots,
                                   cudaStream_t stream) {
-  static bool kv_attr[64] = {false}, q_attr[64] = {false};
-  cudaError_t e = set_smem(bwd::rel_attn_bwd_dkdv_kernel, bwd::kv::kSmemAlloc, kv_attr);
+  static std::atomic<bool> kv_attr[64], q_attr[64];
+  cudaError_t e = set_smem_limit_once(bwd::rel_attn_bwd_dkdv_kernel, bwd::kv::kSmemAlloc, kv_attr);
   if (e != cudaSuccess) return e;
-  e = set_smem(bwd::rel_attn_bwd_dq_kernel, bwd::q::kSmemAlloc, q_attr);
+  e = set_smem_limit_once(bwd::rel_attn_bwd_dq_kernel, bwd::q::kSmemAlloc, q_attr);
   if (e != cudaSuccess) return e;
   const long long rows = args.total_q * args.n_heads;
   if (rows > 0) {

@@ -466,23 +466,12 @@ __global__ void __launch_bounds__(128)
 
 cudaError_t launch_decode_sm100(const DecodeKernelArgs& args, const CUtensorMap& tm_k,
                                 const CUtensorMap& tm_v, cudaStream_t stream) {
-  // The dynamic shared-memory limit is a per-device function attribute.
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaError_t de = cudaGetDevice(&dev);
-  if (de != cudaSuccess) return de;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode::rel_attn_decode_kernel<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(decode::kSmemAlloc));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(decode::rel_attn_decode_kernel<true>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(decode::kSmemAlloc));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_contig[64], attr_paged[64];
+  cudaError_t se = set_smem_limit_once(decode::rel_attn_decode_kernel<false>, decode::kSmemAlloc,
+                                       attr_contig);
+  if (se == cudaSuccess)
+    se = set_smem_limit_once(decode::rel_attn_decode_kernel<true>, decode::kSmemAlloc, attr_paged);
+  if (se != cudaSuccess) return se;
   const int head_blocks = (args.group + args.heads_per_cta - 1) / args.heads_per_cta;
   dim3 grid(args.num_splits, args.kv_heads * head_blocks, args.batch);
   if (args.block_table != nullptr)

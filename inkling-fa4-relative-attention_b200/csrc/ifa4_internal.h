@@ -5,9 +5,30 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace ifa4 {
 
 constexpr int kHeadDim = 128;
+
+// Raises a kernel's dynamic shared-memory limit on the current device, once per device (the
+// limit is a per-device function attribute).  `done` is one flag per device ordinal; it is
+// atomic, so host threads launching at the same time do not race on it (two first calls may
+// both set the attribute, which is harmless: the value is the same).
+template <typename K>
+cudaError_t set_smem_limit_once(K kernel, uint32_t bytes, std::atomic<bool> (&done)[64]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!done[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bytes));
+    if (e != cudaSuccess) return e;
+    done[dev].store(true, std::memory_order_release);
+  }
+  return cudaSuccess;
+}
 
 // Status bits written by kernels that abandoned a bounded wait.
 constexpr int kStatusPrefillTimeout = 1;

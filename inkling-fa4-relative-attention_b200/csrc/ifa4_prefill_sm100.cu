@@ -804,19 +804,10 @@ template <int kEmu, int kHalf2, bool kPaged>
 cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
                            cudaStream_t stream) {
-  // The dynamic shared-memory limit is a per-device function attribute.
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaError_t de = cudaGetDevice(&dev);
-  if (de != cudaSuccess) return de;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(prefill::kSmemAlloc));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[64];
+  cudaError_t e = set_smem_limit_once(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>,
+                                      prefill::kSmemAlloc, attr_set);
+  if (e != cudaSuccess) return e;
   prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>
       <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
   return cudaGetLastError();

@@ -286,18 +286,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
 cudaError_t launch_rel_logits_sm100(const RelLogitsKernelArgs& args, const CUtensorMap& tm_rel,
                                     int grid, cudaStream_t stream) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaError_t de = cudaGetDevice(&dev);
-  if (de != cudaSuccess) return de;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(rl::rel_logits_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(rl::kSmemAlloc));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[64];
+  cudaError_t e = set_smem_limit_once(rl::rel_logits_kernel, rl::kSmemAlloc, attr_set);
+  if (e != cudaSuccess) return e;
   rl::rel_logits_kernel<<<grid, rl::kThreads, rl::kSmemAlloc, stream>>>(args, tm_rel);
   return cudaGetLastError();
 }

@@ -98,9 +98,19 @@ def config_cpu_reference(device="cpu", seed=0) -> Case:
     return c
 
 
+def ragged_batch_lengths(seed=0, n=16, lo=1, hi=4096) -> list:
+    """The sequence lengths of ``config_ragged(seed=seed)``."""
+    return ragged_lengths(n, lo, hi, seed + 1000)
+
+
+def decode_batch_lengths(seed=0, batch=128, lo=1024, hi=32768) -> list:
+    """The K/V lengths of ``config_decode(seed=seed, batch=batch)``."""
+    return ragged_lengths(batch, lo, hi, seed + 2000)
+
+
 def config_ragged(device="cpu", seed=0, n=16, lo=1, hi=4096, gen_device="cpu") -> Case:
     """Config 2: 16 sequences with lengths ~ U[1, 4096], GQA 32/8, R=128."""
-    lens = ragged_lengths(n, lo, hi, seed + 1000)
+    lens = ragged_batch_lengths(seed, n, lo, hi)
     c = make_case(lens, lens, 32, 8, 128, seed=seed, device=device, rel_std=0.5,
                   gen_device=gen_device)
     c.meta.update(name="ragged16_u1_4096_gqa32_8", causal=True)
@@ -128,7 +138,7 @@ def config_chunked(device="cpu", seed=0, n=8, cache=16384, chunk=2048, gen_devic
 def config_decode(device="cpu", seed=0, batch=128, lo=1024, hi=32768, gen_device="cpu") -> Case:
     """Config 5: batch=128 single-token decode, KV lengths ~ U[1024, 32768], GQA 32/8, R=128,
     bottom-right alignment (the query is the last position of its sequence)."""
-    lens = ragged_lengths(batch, lo, hi, seed + 2000)
+    lens = decode_batch_lengths(seed, batch, lo, hi)
     c = make_case([1] * batch, lens, 32, 8, 128, seed=seed, device=device, rel_std=0.5,
                   gen_device=gen_device)
     c.meta.update(name=f"decode{batch}_u{lo}_{hi}", causal=True, causal_align="bottom_right")

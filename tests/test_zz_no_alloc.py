@@ -61,3 +61,48 @@ def test_noalloc_rejects_explicit_splits_beyond_the_static_scratch():
     rc = L.ifa4_decode_launch_noalloc(ctypes.byref(p), None)
     assert rc == _lib.IFA4_ERR_WORKSPACE
     assert b"static scratch" in L.ifa4_last_error_string()
+
+
+def test_noalloc_caps_the_automatic_plan_when_partials_outgrow_the_scratch():
+    """A batch whose automatic split plan needs more partials than the static array holds
+    (128 sequences x 32 heads; the longest sequence asks for 10 chunks of 2048 keys, 21 MB of
+    partials): the entry point caps the split count so that the partials fit, and CTAs then
+    stride over more chunks than there are splits.  Output and log-sum-exp are checked against
+    the workspace entry point on the same capped plan (bit for bit) and on its own uncapped
+    plan (within the test tolerance)."""
+    L = _lib.lib()
+    lens = [20000] + [1024 + 97 * i for i in range(127)]
+    c = make_case([1] * len(lens), lens, 32, 8, 128, seed=41, device="cuda", rel_std=0.5)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nbytes, splits, chunk = _ops.decode_plan(_params(c, torch.empty_like(c.q)))
+    assert nbytes > _lib.NOALLOC_DECODE_SCRATCH_BYTES  # the automatic plan does not fit
+    per_split = len(lens) * 32 * 129 * 4
+    capped = _lib.NOALLOC_DECODE_SCRATCH_BYTES // per_split
+    assert 2 <= capped < splits and max(lens) > capped * chunk  # CTAs stride over chunks
+
+    def lse_buf():
+        return torch.full((32, len(lens)), float("nan"), dtype=torch.float32, device="cuda")
+
+    def with_workspace(num_splits, chunk_len):
+        out, lse = torch.full_like(c.q, float("nan")), lse_buf()
+        p = _params(c, out, num_splits, chunk_len)
+        _ops._fill_lse(p, lse)
+        need, _, _ = _ops.decode_plan(p)
+        ws = torch.empty(max(need, 16), dtype=torch.uint8, device="cuda")
+        _lib.check(L.ifa4_decode_launch(ctypes.byref(p), ctypes.c_void_p(ws.data_ptr()),
+                                        ctypes.c_size_t(need), stream))
+        torch.cuda.synchronize()
+        return out, lse
+
+    ref_out, ref_lse = with_workspace(0, 0)                # uncapped automatic plan
+    cap_out, cap_lse = with_workspace(int(capped), chunk)  # the plan the no-alloc call uses
+    for _ in range(2):
+        out, lse = torch.full_like(c.q, float("nan")), lse_buf()
+        p = _params(c, out)
+        _ops._fill_lse(p, lse)
+        _lib.check(L.ifa4_decode_launch_noalloc(ctypes.byref(p), stream))
+        torch.cuda.synchronize()
+        assert _lib.read_device_status(stream.value or 0) == 0
+        assert torch.equal(out, cap_out) and torch.equal(lse, cap_lse)
+        torch.testing.assert_close(out.float(), ref_out.float(), atol=ATOL, rtol=RTOL)
+        torch.testing.assert_close(lse, ref_lse, atol=2e-3, rtol=1e-4)
