@@ -438,27 +438,37 @@ def timed(fn, steps, warmup, stream, dist=None, barrier=None):
     return ms, med
 
 
-def read_stream_peak(dev):
-    """A read-only HBM stream on this GPU, measured in the run: torch's sum over a 4 GiB bf16
-    buffer (best of 10, CUDA events).  Decode reads ~99 % and writes ~1 % of its bytes, so its
-    natural ceiling is a read stream, which runs faster than the read+write copy of
-    MEASURED_PEAKS.json."""
+def read_stream_peak(dev, stream):
+    """The read-only HBM stream ceiling of this GPU, measured in the run: the library's
+    measurement hook (16-byte non-coherent loads, four in flight per thread) over a 4 GiB
+    buffer, best of 10 after 3 warm-up passes, CUDA events on the launching stream.  Decode
+    reads ~99 % and writes ~1 % of its bytes, so a read stream, not the read+write copy of
+    MEASURED_PEAKS.json, is its ceiling."""
+    import ctypes
+
     import torch
 
-    x = torch.ones(1 << 31, dtype=torch.bfloat16, device=dev)
+    from inkling_fa4 import _lib
+
+    L = _lib.lib()
+    nbytes = 4 << 30
+    x = torch.ones(nbytes // 2, dtype=torch.bfloat16, device=dev)
+    sink = torch.zeros(1, dtype=torch.int32, device=dev)
+    h = ctypes.c_void_p(stream.cuda_stream)
     best = float("inf")
     for i in range(13):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        x.sum()
-        b.record()
+        a.record(stream)
+        _lib.check(L.ifa4_measure_read_stream(ctypes.c_void_p(x.data_ptr()),
+                                              ctypes.c_size_t(nbytes),
+                                              ctypes.c_void_p(sink.data_ptr()), h))
+        b.record(stream)
         torch.cuda.synchronize()
         if i >= 3:
             best = min(best, a.elapsed_time(b))
-    gbs = x.numel() * 2 / (best / 1e3) / 1e9
-    del x
+    del x, sink
     torch.cuda.empty_cache()
-    return gbs
+    return nbytes / (best / 1e3) / 1e9
 
 
 def main():
@@ -857,6 +867,24 @@ def main():
         diff = float((full.float() - ref.float()).abs().max().item())
         ok = torch.tensor([1 if torch.equal(full, ref) else 0], device=dev)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        # the same split with the output assembled during the call: each rank's kernel stores its
+        # heads' finished rows into every rank's output buffer (CUDA IPC mappings), then one
+        # one-element all-reduce orders the reads
+        from inkling_fa4.sharding import PeerOutputs, prefill_to_all_ranks
+
+        peers = PeerOutputs((S, HQ, D), dtype=torch.bfloat16, device=dev)
+        fused_step = lambda: prefill_to_all_ranks(peers, sh, q_s, k_s, v_s, rel_s, sc.cu_q,
+                                                  sc.cu_k, S, S, R)
+        peers.local.fill_(float("nan"))
+        peers.barrier()
+        ms_f, _ = timed(fused_step, args.steps, args.warmup, stream, dist, barrier)
+        peers.local.fill_(float("nan"))  # every element must come from this call's stores
+        peers.barrier()
+        fused = fused_step()
+        torch.cuda.synchronize()
+        fdiff = float((fused.float() - ref.float()).abs().max().item())
+        fok = torch.tensor([1 if torch.equal(fused, ref) else 0], device=dev)
+        dist.all_reduce(fok, op=dist.ReduceOp.MIN)
         full_flops = 4 * D * HQ * visible_pairs_causal(S)
         # NCCL's own time for the 32 MB-per-rank all-gather alone (the output of this rank)
         src = torch.empty((S, sh.n_q, D), dtype=torch.bfloat16, device=dev)
@@ -871,6 +899,14 @@ def main():
             "ms_per_step_no_gather": ms_ng / args.steps,
             "ms_per_step_with_gather": ms_g / args.steps,
             "parity_ok": bool(ok.item() == 1), "max_abs_diff_vs_unsharded": diff,
+            "value_with_peer_stores": full_flops * args.steps / (ms_f / 1e3) / 1e12,
+            "ms_per_step_with_peer_stores": ms_f / args.steps,
+            "peer_stores_parity_ok": bool(fok.item() == 1),
+            "peer_stores_max_abs_diff_vs_unsharded": fdiff,
+            "peer_stores": "each rank's prefill kernel stores its heads' output rows into every "
+                           "rank's [T, 32, 128] buffer (CUDA IPC peer mappings, plain 16-byte "
+                           "stores over NVLink) as its tiles finish; one 4-byte NCCL all-reduce "
+                           "per step orders the reads",
             "nccl_all_gather_alone": {"ms": ag_ms / args.steps,
                                       "bus_gbs": ag_bytes * (world - 1) / world
                                       / (ag_ms / args.steps / 1e3) / 1e9,
@@ -880,7 +916,7 @@ def main():
                        "collective": "one NCCL all_gather_into_tensor of the output heads "
                                      f"({S * HQ * D * 2 >> 20} MB assembled per step)"},
             "gpu_launches": args.steps}
-        del sc, q_s, k_s, v_s, rel_s, full, ref, src, gbuf
+        del sc, q_s, k_s, v_s, rel_s, full, ref, src, gbuf, fused, peers
         torch.cuda.empty_cache()
 
         # config 5 decode with its KV heads split 8/N per rank (same batch on every rank)
@@ -930,7 +966,7 @@ def main():
 
     # ---------------- config 5: batched decode (contiguous and paged)
     if want("decode"):
-        read_gbs = read_stream_peak(dev)
+        read_gbs = read_stream_peak(dev, stream)
         dc = config_decode(device=dev, seed=rank, batch=args.decode_batch, gen_device=dev)
         lens = dc.seqlens_k
         kv_bytes = sum(lens) * HKV * D * 2 * 2
@@ -954,8 +990,8 @@ def main():
         def hbm_roofline(achieved):
             return {"bound": "hbm", "achieved": achieved, "peak": read_gbs, "unit": "GB/s",
                     "frac": achieved / read_gbs,
-                    "peak_source": "read-only stream measured in this run (torch sum over a "
-                                   "4 GiB bf16 buffer, best of 10)",
+                    "peak_source": "read-only stream measured in this run "
+                                   "(ifa4_measure_read_stream over 4 GiB, best of 10)",
                     "frac_of_copy_peak": achieved / peaks["hbm_gbs"],
                     "copy_peak": peaks["hbm_gbs"],
                     "copy_peak_source": f"hbm_gbs (read+write copy) of {peak_kind}",

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define IFA4_ABI_VERSION 5
+#define IFA4_ABI_VERSION 6
 
 enum {
   IFA4_OK = 0,
@@ -101,7 +101,22 @@ typedef struct IFA4PrefillParams {
   int64_t k_stride_page, v_stride_page;
   int32_t page_size;
   int32_t num_pages;
+  /* Optional copies of the output on other GPUs (ABI version 6; not in the reference, whose
+   * single-GPU call has no multi-GPU path).  When n_out_peers > 0, out_peers is a host array of
+   * n_out_peers device addresses, valid in this process, each pointing at the element that
+   * corresponds to out[0] in another buffer laid out exactly like the one out points into
+   * (typically another GPU's output buffer mapped into this process by CUDA IPC).  The kernel
+   * stores every output row to out and, at the same offset, to each of these buffers as its
+   * tiles finish, so ranks that each compute some heads of one call assemble the whole output on
+   * every GPU during the call, with no gather afterwards.  Plain 16-byte stores (no TMA, no
+   * multicast); 16-byte aligned addresses; at most IFA4_MAX_OUT_PEERS.  The writes are complete
+   * when the launch completes; the caller orders the other GPUs' reads after that (a barrier in
+   * stream order) and keeps them from reading while a later call overwrites the buffers. */
+  const void* const* out_peers;
+  int32_t n_out_peers;
 } IFA4PrefillParams;
+
+#define IFA4_MAX_OUT_PEERS 7
 
 /* Prefill.  Replaces the per-sequence launch loop of inkling_fa4_rel_attention_triton
  * (src/inkling_fa4/triton_kernel.py:84-106) and of the KV-pruned variant
@@ -289,6 +304,14 @@ int ifa4_rel_logits_launch(const IFA4RelLogitsParams* params, void* stream);
  * Run it alone: while the status word is nonzero, concurrently running kernels of this library
  * abandon their waits too (that is how one failure stops the others). */
 int ifa4_selftest_bounded_wait(int64_t timeout_ns, void* stream);
+
+/* Measurement hook (no counterpart in the reference): launches on `stream` one read-only pass
+ * over `bytes` bytes at `buf` (16-byte aligned, bytes a multiple of 16) with 16-byte
+ * non-coherent loads, four in flight per thread, 4 CTAs of 512 threads per SM.  Timing it gives
+ * the HBM read-stream ceiling against which the decode kernel (about 99 % reads) is judged.
+ * `sink` is a device word that is written only in the unlikely event that the folded data
+ * equal a fixed constant. */
+int ifa4_measure_read_stream(const void* buf, size_t bytes, uint32_t* sink, void* stream);
 
 /* Reads (and optionally clears) the library's device status word on `stream`, blocking the
  * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on

@@ -60,6 +60,28 @@ __global__ void __launch_bounds__(64) ifa4_selftest_wait_kernel(int* status,
   if (threadIdx.x == 0) ifa4::mbar_arrive(&bar);  // complete the phase before the CTA exits
 }
 
+// Read-only HBM stream (measurement hook): every thread keeps four 16-byte non-coherent loads
+// in flight per iteration over a grid-strided range and folds them into one word, which is
+// written out only if it equals an unlikely constant (so the loads cannot be dropped).
+__global__ void __launch_bounds__(512) ifa4_read_stream_kernel(const uint4* __restrict__ src,
+                                                               unsigned long long n16,
+                                                               uint32_t* sink) {
+  const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+  unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  uint32_t acc = 0;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    const uint4 a = ifa4::ldg_nc_v4(src + i), b = ifa4::ldg_nc_v4(src + i + stride);
+    const uint4 c = ifa4::ldg_nc_v4(src + i + 2 * stride), d = ifa4::ldg_nc_v4(src + i + 3 * stride);
+    acc ^= (a.x ^ a.y ^ a.z ^ a.w) ^ (b.x ^ b.y ^ b.z ^ b.w) ^ (c.x ^ c.y ^ c.z ^ c.w) ^
+           (d.x ^ d.y ^ d.z ^ d.w);
+  }
+  for (; i < n16; i += stride) {
+    const uint4 a = ifa4::ldg_nc_v4(src + i);
+    acc ^= a.x ^ a.y ^ a.z ^ a.w;
+  }
+  if (acc == 0x9e3779b9u) atomicAdd(sink, 1u);
+}
+
 constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {nullptr};
 int g_sm_count[kMaxDevices] = {0};
@@ -329,6 +351,23 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   a.v_sh = p->v_stride_h;
   a.v_sp = p->v_stride_page;
   a.status = status;
+  if (p->n_out_peers < 0 || p->n_out_peers > IFA4_MAX_OUT_PEERS)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "prefill: n_out_peers %d outside [0, %d]",
+                p->n_out_peers, IFA4_MAX_OUT_PEERS);
+  if (p->n_out_peers > 0 && p->out_peers == nullptr)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "prefill: out_peers is NULL");
+  if (p->n_out_peers > 0 && (p->block_table != nullptr || p->tile_config != 0))
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: out_peers needs contiguous K/V and tile_config 0");
+  a.n_out_peers = p->n_out_peers;
+  for (int i = 0; i < p->n_out_peers; ++i) {
+    const void* pp = p->out_peers[i];
+    if (pp == nullptr || !aligned16(pp))
+      return fail(IFA4_ERR_INVALID_ARGUMENT, "prefill: out_peers[%d] must be a 16-byte aligned "
+                  "device address", i);
+    // byte distance in elements (both addresses are 16-byte aligned)
+    a.out_peer_delta[i] = (reinterpret_cast<intptr_t>(pp) - reinterpret_cast<intptr_t>(p->out)) /
+                          static_cast<intptr_t>(sizeof(uint16_t));
+  }
 
   CUtensorMap tq, tk, tv;
   if ((rc = encode_rows_heads_dims(&tq, p->q, p->total_q, p->n_heads, p->q_stride_t,
@@ -850,6 +889,22 @@ int ifa4_selftest_bounded_wait(int64_t timeout_ns, void* stream) {
       status, static_cast<unsigned long long>(timeout_ns));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return IFA4_OK;
+}
+
+int ifa4_measure_read_stream(const void* buf, size_t bytes, uint32_t* sink, void* stream) {
+  g_last_error[0] = '\0';
+  if (buf == nullptr || sink == nullptr || bytes == 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "read_stream: null buffer or sink, or zero bytes");
+  if ((reinterpret_cast<uintptr_t>(buf) & 15u) != 0 || (bytes & 15u) != 0)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "read_stream: buffer and size must be 16-byte aligned");
+  int sms = 148;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  ifa4_read_stream_kernel<<<sms * 4, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(buf), static_cast<unsigned long long>(bytes / 16), sink);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "read_stream launch");
   return IFA4_OK;
 }
 

@@ -64,6 +64,9 @@ struct PrefillKernelArgs {
   const uint16_t* v;         // V cache base (partial last unit copied with plain loads)
   long long v_st, v_sh, v_sp;
   int* status;
+  // output copies on other GPUs: element e of out is also stored at out + out_peer_delta[i] + e
+  long long out_peer_delta[7];
+  int n_out_peers;
 };
 
 struct PrefillLaunch {

@@ -259,7 +259,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint3
   }
 }
 
-template <int kEmu, int kHalf2, bool kPaged>
+template <int kEmu, int kHalf2, bool kPaged, bool kPeers>
 __global__ void __launch_bounds__(kThreads, 1)
     rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
                             const __grid_constant__ CUtensorMap tm_q,
@@ -781,6 +781,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint16_t* dst = a.out + static_cast<long long>(q_start + qr) * a.out_st +
                             static_cast<long long>(h) * a.out_sh + g * 8;
             *reinterpret_cast<uint4*>(dst) = val;
+            if (kPeers) {  // the same row in other GPUs' outputs
+              for (int pr = 0; pr < a.n_out_peers; ++pr)
+                *reinterpret_cast<uint4*>(dst + a.out_peer_delta[pr]) = val;
+            }
           }
         }
       }
@@ -789,6 +793,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // stores to other GPUs' outputs are performed system-wide before the CTA retires
+  if (kPeers && warp >= 4) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
@@ -800,15 +806,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace prefill
 
 namespace {
-template <int kEmu, int kHalf2, bool kPaged>
+template <int kEmu, int kHalf2, bool kPaged, bool kPeers = false>
 cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
                            cudaStream_t stream) {
   static std::atomic<bool> attr_set[64];
-  cudaError_t e = set_smem_limit_once(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>,
-                                      prefill::kSmemAlloc, attr_set);
+  cudaError_t e =
+      set_smem_limit_once(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kPeers>,
+                          prefill::kSmemAlloc, attr_set);
   if (e != cudaSuccess) return e;
-  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged>
+  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kPeers>
       <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
   return cudaGetLastError();
 }
@@ -844,6 +851,10 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
     // lose 4 % at 32k.
     emu = 2;
     h2 = 0;
+  }
+  if (args.n_out_peers > 0) {  // output copies on other GPUs: contiguous K/V, automatic choice
+    if (args.block_table != nullptr || emu != 2 || h2 != 0) return cudaErrorInvalidValue;
+    return launch_variant<2, 0, false, true>(args, tm_q, tm_k, tm_v, grid, stream);
   }
   if (args.block_table != nullptr) {  // paged cache: the automatic choice and its neighbours
     if (emu == 0 && h2 == 0) return launch_variant<0, 0, true>(args, tm_q, tm_k, tm_v, grid, stream);

@@ -19,7 +19,8 @@ IFA4_ERR_DEVICE_TIMEOUT = -5
 IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0
-ABI_VERSION = 5
+ABI_VERSION = 6
+MAX_OUT_PEERS = 7
 NOALLOC_DECODE_SCRATCH_BYTES = 16 * 1024 * 1024
 
 EXPORTED_SYMBOLS = (
@@ -32,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "ifa4_rel_logits_launch",
     "ifa4_read_device_status",
     "ifa4_selftest_bounded_wait",
+    "ifa4_measure_read_stream",
     "ifa4_prefill_tile_config_name",
     "ifa4_last_error_string",
     "ifa4_abi_version",
@@ -62,6 +64,7 @@ class PrefillParams(ctypes.Structure):
         ("block_table", ctypes.c_void_p), ("block_table_stride", ctypes.c_int64),
         ("k_stride_page", ctypes.c_int64), ("v_stride_page", ctypes.c_int64),
         ("page_size", ctypes.c_int32), ("num_pages", ctypes.c_int32),
+        ("out_peers", ctypes.POINTER(ctypes.c_void_p)), ("n_out_peers", ctypes.c_int32),
     ]
 
 
@@ -146,6 +149,8 @@ def lib() -> ctypes.CDLL:
     L.ifa4_rel_logits_launch.restype = ctypes.c_int
     L.ifa4_selftest_bounded_wait.argtypes = [ctypes.c_int64, vp]
     L.ifa4_selftest_bounded_wait.restype = ctypes.c_int
+    L.ifa4_measure_read_stream.argtypes = [vp, sz, vp, vp]
+    L.ifa4_measure_read_stream.restype = ctypes.c_int
     L.ifa4_read_device_status.argtypes = [vp, i32, ctypes.POINTER(i32)]
     L.ifa4_read_device_status.restype = ctypes.c_int
     L.ifa4_prefill_tile_config_name.argtypes = [i32]

@@ -171,7 +171,10 @@ def _table(block_table):
 def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
             rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
             head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
-            tile_config=0, return_lse=False, lse=None, block_table=None):
+            tile_config=0, return_lse=False, lse=None, block_table=None, out_peers=None):
+    """``out_peers``: optional device addresses (valid in this process) of the element that
+    corresponds to ``out[0, 0, 0]`` in other GPUs' output buffers laid out like ``out``'s; the
+    kernel stores every output row there too (see ``inkling_fa4.sharding.PeerOutputs``)."""
     block_table = _table(block_table)
     q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
         "prefill", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
@@ -184,6 +187,13 @@ def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_s
     p.max_seqlen_q = int(max_seqlen_q) if max_seqlen_q else 0
     p.softmax_scale = scale
     p.tile_config = int(tile_config)
+    peers = None
+    if out_peers:
+        if len(out_peers) > _lib.MAX_OUT_PEERS:
+            raise ValueError(f"prefill: at most {_lib.MAX_OUT_PEERS} out_peers")
+        peers = (ctypes.c_void_p * len(out_peers))(*[int(x) for x in out_peers])
+        p.out_peers = ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p))
+        p.n_out_peers = len(out_peers)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         _lib.check(_lib.lib().ifa4_prefill_launch(ctypes.byref(p), ctypes.c_void_p(stream)))

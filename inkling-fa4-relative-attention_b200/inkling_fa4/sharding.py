@@ -4,12 +4,17 @@ The path shards with no exchange during compute:
 
 * by KV-head group: rank r of n owns kv heads [r*Hkv/n, (r+1)*Hkv/n) and their query heads
   [r*Hq/n, (r+1)*Hq/n); it runs the kernels on head slices of q/k/v/rel (views, no copies:
-  the kernels take arbitrary head strides) for all sequences.  The only collective is the
-  optional all-gather of the output heads (``gather_heads``), over NCCL / NVLink.
+  the kernels take arbitrary head strides) for all sequences.  The full output reaches every
+  rank either through the all-gather of the output heads (``gather_heads``, NCCL over
+  NVLink, then a head-interleaving copy) or, for the prefill, during the call itself
+  (``prefill_to_all_ranks``): each rank's kernel stores its heads' rows into every rank's
+  output buffer (``PeerOutputs``, mapped with CUDA IPC) as its tiles finish, and one small
+  all-reduce afterwards orders the other ranks' reads after those stores.
 * by sequence: ``balance_sequences`` splits a ragged batch into n groups of nearly equal
   token count (for decode, nearly equal KV bytes); each rank runs its sequences.
 
-Nothing here reads another GPU's memory; each rank's kernels only touch local tensors.
+No kernel reads another GPU's memory; the only remote accesses are the plain 16-byte stores
+of finished output rows (no TMA, no multicast).
 """
 from __future__ import annotations
 
@@ -104,3 +109,68 @@ def select_sequences(idx, cu_q, cu_k, *tensors_q_k):
     rq, rk = rows_q.to(dev), rows_k.to(dev)
     return (q.index_select(0, rq), rel.index_select(0, rq), k.index_select(0, rk),
             v.index_select(0, rk), new_cq.to(dev), new_ck.to(dev))
+
+
+class PeerOutputs:
+    """One output buffer of the same shape on every rank, each rank's buffer mapped into every
+    other rank's address space with CUDA IPC (torch's CUDA storage sharing: cudaIpcGetMemHandle
+    / cudaIpcOpenMemHandle, a plain peer mapping over NVLink, no multicast object).  Collective:
+    every rank of ``group`` constructs it with the same shape.  ``local`` is this rank's buffer;
+    ``peer_ptrs(view)`` gives, for a view into ``local``, the addresses of the same elements in
+    the other ranks' buffers (valid in this process)."""
+
+    def __init__(self, shape, dtype=torch.bfloat16, device=None, group=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.local = torch.empty(shape, dtype=dtype, device=device)
+        info = self.local.untyped_storage()._share_cuda_()
+        infos = [None] * self.world
+        dist.all_gather_object(infos, info, group=group)
+        self._mapped = []  # keeps the other ranks' mapped storages open
+        self.bases = []
+        for r, (dev, handle, size, offset, rc_handle, rc_offset, ev_handle, ev_sync) in \
+                enumerate(infos):
+            if r == self.rank:
+                self.bases.append(self.local.data_ptr())
+                continue
+            st = torch.UntypedStorage._new_shared_cuda(dev, handle, size, offset, rc_handle,
+                                                       rc_offset, ev_handle, ev_sync)
+            self._mapped.append(st)
+            self.bases.append(st.data_ptr())
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.local.device)
+
+    def peer_ptrs(self, view: torch.Tensor):
+        """Addresses, in the other ranks' buffers, of the element ``view`` starts at."""
+        off = view.data_ptr() - self.local.data_ptr()
+        if not 0 <= off < self.local.numel() * self.local.element_size():
+            raise ValueError("view does not start inside this rank's buffer")
+        return [b + off for r, b in enumerate(self.bases) if r != self.rank]
+
+    def barrier(self):
+        """Stream-ordered barrier over the ranks (a one-element NCCL all-reduce on the current
+        stream): once it completes on a rank, every rank's earlier launches on its stream (and
+        so their stores into this rank's buffer) have completed."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+
+def prefill_to_all_ranks(peers: PeerOutputs, sh: HeadShard, q, k, v, rel, cu_seqlens_q,
+                         cu_seqlens_k, max_seqlen_q, max_seqlen_k, rel_extent, **kw):
+    """Head-sharded prefill whose output assembles itself on every rank: rank ``sh.rank``
+    computes its query heads ``[sh.q_lo, sh.q_hi)`` from its slices of the inputs (as
+    ``shard_tensors`` gives them) and its kernel stores each finished output row both into its
+    own ``peers.local[:, q_lo:q_hi]`` and into the same heads of every other rank's buffer.
+    After the stream-ordered barrier every rank's ``peers.local`` holds all heads.  Collective
+    (every rank calls it); the caller keeps ranks from reading ``peers.local`` while a later call
+    writes it (e.g. by calling the barrier before reusing the buffer)."""
+    from . import _ops
+
+    view = peers.local[:, sh.q_lo:sh.q_hi]
+    _ops.prefill(q, k, v, rel, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                 rel_extent, out=view, out_peers=peers.peer_ptrs(view), **kw)
+    peers.barrier()
+    return peers.local

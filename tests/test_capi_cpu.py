@@ -198,3 +198,11 @@ def test_selftest_limit_validated_before_any_cuda_call():
     L = _lib.lib()
     assert L.ifa4_selftest_bounded_wait(0, None) == _lib.IFA4_ERR_INVALID_ARGUMENT
     assert b"timeout_ns" in L.ifa4_last_error_string()
+
+
+def test_read_stream_hook_validates_before_any_cuda_call():
+    L = _lib.lib()
+    assert L.ifa4_measure_read_stream(None, 16, None, None) == _lib.IFA4_ERR_INVALID_ARGUMENT
+    # misaligned size, with non-null (never dereferenced) pointers
+    assert L.ifa4_measure_read_stream(16, 24, 16, None) == _lib.IFA4_ERR_INVALID_ARGUMENT
+    assert b"16-byte" in L.ifa4_last_error_string()

@@ -1,7 +1,9 @@
 """KV-head-group sharding on 2 GPUs (one process per GPU, NCCL): each rank runs the prefill and
 decode kernels on its head slices (views of the full tensors), the output heads are
-all-gathered, and the result must equal the unsharded single-GPU computation bit for bit
-(the per-head computation is identical).  Skipped on boxes with fewer than 2 GPUs."""
+all-gathered (or, for the prefill, stored by each rank's kernel into every rank's output
+buffer through CUDA IPC mappings), and the result must equal the unsharded single-GPU
+computation bit for bit (the per-head computation is identical).  Skipped on boxes with fewer
+than 2 GPUs."""
 import os
 import socket
 
@@ -27,7 +29,8 @@ def _rank_main(rank, world, port, q_out):
 
     from inkling_fa4 import (inkling_fa4_rel_attention_decode_triton,
                              inkling_fa4_rel_attention_triton)
-    from inkling_fa4.sharding import gather_heads, head_shard, shard_tensors
+    from inkling_fa4.sharding import (PeerOutputs, gather_heads, head_shard,
+                                      prefill_to_all_ranks, shard_tensors)
     from inkling_fa4.workloads import make_case
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -42,6 +45,14 @@ def _rank_main(rank, world, port, q_out):
         q, k, v, rel = shard_tensors(sh, c.q, c.k, c.v, c.rel)
         part = inkling_fa4_rel_attention_triton(q, k, v, rel, c.cu_q, c.cu_k, 1000, 1000, 128)
         full = gather_heads(part, world)
+        peers = PeerOutputs(tuple(c.q.shape), device=dev)
+        peers.local.fill_(float("nan"))  # every element must come from the kernels' stores
+        peers.barrier()
+        fused = []
+        for _ in range(2):  # the second call overwrites the buffers the first one filled
+            fused.append(prefill_to_all_ranks(peers, sh, q, k, v, rel, c.cu_q, c.cu_k, 1000, 1000,
+                                              128).clone())
+            peers.barrier()
         d = make_case([1] * 4, [3000, 70, 5000, 640], 16, 4, 128, seed=78, device=dev)
         dq, dk, dv, drel = shard_tensors(sh, d.q, d.k, d.v, d.rel)
         # a fixed split plan keeps the per-head arithmetic identical to the unsharded call
@@ -56,7 +67,8 @@ def _rank_main(rank, world, port, q_out):
             dref = inkling_fa4_rel_attention_decode_triton(d.q, d.k, d.v, d.rel, d.cu_q, d.cu_k, 1,
                                                            5000, 128, causal_align="bottom_right",
                                                            num_splits=4, chunk_len=512)
-            q_out.put((bool(torch.equal(full, ref)), bool(torch.equal(dfull, dref))))
+            q_out.put((bool(torch.equal(full, ref)), bool(torch.equal(dfull, dref)),
+                       all(bool(torch.equal(f, ref)) for f in fused)))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -70,8 +82,8 @@ def test_head_sharded_prefill_and_decode_on_two_gpus():
     procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q_out)) for r in range(2)]
     for p in procs:
         p.start()
-    same_prefill, same_decode = q_out.get(timeout=300)
+    same_prefill, same_decode, same_peer_stores = q_out.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert same_prefill and same_decode
+    assert same_prefill and same_decode and same_peer_stores

@@ -223,3 +223,46 @@ def test_running_max_growth_inside_interior_tiles(jump):
         out = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, c.max_q, c.max_k, 128,
                            tile_config=tc)
         assert_close(np32(out)[toks], want, what=f"tile_config {tc}")
+
+
+@pytest.mark.parametrize("scale", [60.0, 3000.0])
+@pytest.mark.parametrize("tile_config", [0, 1, 3])
+@pytest.mark.parametrize("window", [None, 511])
+def test_band_tiles_with_scores_far_above_the_running_max(scale, tile_config, window):
+    """Band tiles (relative bias on every one of them at R = 1024) and window-boundary tiles
+    also take the single pass against the running max; keys scaled up near each row's diagonal
+    push their scores far above it, so those tiles must be redone with their true max."""
+    from inkling_fa4.workloads import Case
+    c = make_case([2048, 1500], [2048, 1500], 8, 2, 1024, seed=int(scale) + 7, rel_std=2.0)
+    k = c.k.float()
+    k[1500:1700] *= scale
+    k[2048 + 900:2048 + 1000] *= scale
+    c = Case(q=c.q, k=k.to(torch.bfloat16), v=c.v, rel=c.rel, cu_q=c.cu_q, cu_k=c.cu_k,
+             seqlens_q=c.seqlens_q, seqlens_k=c.seqlens_k, rel_extent=1024)
+    c = to_dev(c)
+    toks, want = oracle_rows(c, 48, [0, 3, 5], 1 / 128, window_left=window, seed=int(scale) + 2)
+    from inkling_fa4 import _ops
+    out = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, c.max_q, c.max_k, 1024,
+                       window_size=(-1 if window is None else window, 0), tile_config=tile_config)
+    assert_close(np32(out)[:, [0, 3, 5]][toks], want, what=f"tile_config {tile_config}")
+    assert torch.isfinite(out.float()).all()
+
+
+def test_window_rows_whose_first_keys_are_far_below_zero():
+    """Rows whose first visible KV tile (the window's left edge) comes after a tile they see
+    nothing of enter the single pass with no running max yet; if all their scores in that tile
+    are far below 0 (about -185 in log2 units), every p underflows, and the tile must be redone
+    with its true max rather than kept as zero."""
+    from inkling_fa4.workloads import Case
+    c = make_case([1024], [1024], 4, 2, 512, seed=21)
+    u = torch.randn(128, generator=torch.Generator().manual_seed(5))
+    q, k = c.q.float(), c.k.float()
+    q[450:700] = u           # every head of these rows
+    k[200:330] = -128.0 * u  # q.k / 128 = -|u|^2, about -128 (-185 in log2 units)
+    c = Case(q=q.to(torch.bfloat16), k=k.to(torch.bfloat16), v=c.v, rel=c.rel, cu_q=c.cu_q,
+             cu_k=c.cu_k, seqlens_q=c.seqlens_q, seqlens_k=c.seqlens_k, rel_extent=512)
+    c = to_dev(c)
+    for window in (300, 250):
+        out = run_prefill(c, window_size=(window, 0))
+        want = oracle_full(c, 1 / 128, window_left=window)
+        assert_close(np32(out), want, what=f"window {window}")
