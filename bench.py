@@ -487,6 +487,9 @@ def main():
                     help="'headline', or one leg name (profiling runs); 'all' runs everything")
     ap.add_argument("--no-shard", action="store_true",
                     help="skip the head-sharded legs (N > 1 only)")
+    ap.add_argument("--peer-stores", type=int, default=0,
+                    help="N > 1: also time the head-sharded prefill whose kernel stores its rows "
+                         "into every rank's output (1) or not (0)")
     ap.add_argument("--prefill-seq", type=int, default=SEQ,
                     help="sequence length of the headline workload (32768 = BASELINE config 3)")
     ap.add_argument("--tile-config", type=int, default=0,
@@ -870,21 +873,23 @@ def main():
         # the same split with the output assembled during the call: each rank's kernel stores its
         # heads' finished rows into every rank's output buffer (CUDA IPC mappings), then one
         # one-element all-reduce orders the reads
-        from inkling_fa4.sharding import PeerOutputs, prefill_to_all_ranks
+        fused = peers = None
+        if args.peer_stores:
+            from inkling_fa4.sharding import PeerOutputs, prefill_to_all_ranks
 
-        peers = PeerOutputs((S, HQ, D), dtype=torch.bfloat16, device=dev)
-        fused_step = lambda: prefill_to_all_ranks(peers, sh, q_s, k_s, v_s, rel_s, sc.cu_q,
-                                                  sc.cu_k, S, S, R)
-        peers.local.fill_(float("nan"))
-        peers.barrier()
-        ms_f, _ = timed(fused_step, args.steps, args.warmup, stream, dist, barrier)
-        peers.local.fill_(float("nan"))  # every element must come from this call's stores
-        peers.barrier()
-        fused = fused_step()
-        torch.cuda.synchronize()
-        fdiff = float((fused.float() - ref.float()).abs().max().item())
-        fok = torch.tensor([1 if torch.equal(fused, ref) else 0], device=dev)
-        dist.all_reduce(fok, op=dist.ReduceOp.MIN)
+            peers = PeerOutputs((S, HQ, D), dtype=torch.bfloat16, device=dev)
+            fused_step = lambda: prefill_to_all_ranks(peers, sh, q_s, k_s, v_s, rel_s, sc.cu_q,
+                                                      sc.cu_k, S, S, R)
+            peers.local.fill_(float("nan"))
+            peers.barrier()
+            ms_f, _ = timed(fused_step, args.steps, args.warmup, stream, dist, barrier)
+            peers.local.fill_(float("nan"))  # every element must come from this call's stores
+            peers.barrier()
+            fused = fused_step()
+            torch.cuda.synchronize()
+            fdiff = float((fused.float() - ref.float()).abs().max().item())
+            fok = torch.tensor([1 if torch.equal(fused, ref) else 0], device=dev)
+            dist.all_reduce(fok, op=dist.ReduceOp.MIN)
         full_flops = 4 * D * HQ * visible_pairs_causal(S)
         # NCCL's own time for the 32 MB-per-rank all-gather alone (the output of this rank)
         src = torch.empty((S, sh.n_q, D), dtype=torch.bfloat16, device=dev)
@@ -899,14 +904,6 @@ def main():
             "ms_per_step_no_gather": ms_ng / args.steps,
             "ms_per_step_with_gather": ms_g / args.steps,
             "parity_ok": bool(ok.item() == 1), "max_abs_diff_vs_unsharded": diff,
-            "value_with_peer_stores": full_flops * args.steps / (ms_f / 1e3) / 1e12,
-            "ms_per_step_with_peer_stores": ms_f / args.steps,
-            "peer_stores_parity_ok": bool(fok.item() == 1),
-            "peer_stores_max_abs_diff_vs_unsharded": fdiff,
-            "peer_stores": "each rank's prefill kernel stores its heads' output rows into every "
-                           "rank's [T, 32, 128] buffer (CUDA IPC peer mappings, plain 16-byte "
-                           "stores over NVLink) as its tiles finish; one 4-byte NCCL all-reduce "
-                           "per step orders the reads",
             "nccl_all_gather_alone": {"ms": ag_ms / args.steps,
                                       "bus_gbs": ag_bytes * (world - 1) / world
                                       / (ag_ms / args.steps / 1e3) / 1e9,
@@ -916,6 +913,16 @@ def main():
                        "collective": "one NCCL all_gather_into_tensor of the output heads "
                                      f"({S * HQ * D * 2 >> 20} MB assembled per step)"},
             "gpu_launches": args.steps}
+        if args.peer_stores:
+            result["head_sharded32k"].update({
+                "value_with_peer_stores": full_flops * args.steps / (ms_f / 1e3) / 1e12,
+                "ms_per_step_with_peer_stores": ms_f / args.steps,
+                "peer_stores_parity_ok": bool(fok.item() == 1),
+                "peer_stores_max_abs_diff_vs_unsharded": fdiff,
+                "peer_stores": "each rank's prefill kernel stores its heads' output rows into "
+                               "every rank's [T, 32, 128] buffer (CUDA IPC peer mappings, plain "
+                               "16-byte stores over NVLink) as its tiles finish; one 4-byte NCCL "
+                               "all-reduce per step orders the reads"})
         del sc, q_s, k_s, v_s, rel_s, full, ref, src, gbuf, fused, peers
         torch.cuda.empty_cache()
 

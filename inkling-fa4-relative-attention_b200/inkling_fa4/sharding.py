@@ -131,13 +131,19 @@ class PeerOutputs:
         dist.all_gather_object(infos, info, group=group)
         self._mapped = []  # keeps the other ranks' mapped storages open
         self.bases = []
-        for r, (dev, handle, size, offset, rc_handle, rc_offset, ev_handle, ev_sync) in \
+        local_dev = self.local.device.index
+        for r, (_dev, handle, size, offset, rc_handle, rc_offset, ev_handle, _ev_sync) in \
                 enumerate(infos):
             if r == self.rank:
                 self.bases.append(self.local.data_ptr())
                 continue
-            st = torch.UntypedStorage._new_shared_cuda(dev, handle, size, offset, rc_handle,
-                                                       rc_offset, ev_handle, ev_sync)
+            # Opened with this rank's own device current: cudaIpcOpenMemHandle maps the other
+            # GPU's allocation into this device's context and enables this device's peer access
+            # to it, so this device's kernels can store there.  (Opening it under the owner's
+            # device index would map it into a context this device's kernels do not run in.)
+            # No IPC event wait: the ranks order their accesses with barriers.
+            st = torch.UntypedStorage._new_shared_cuda(local_dev, handle, size, offset,
+                                                       rc_handle, rc_offset, ev_handle, False)
             self._mapped.append(st)
             self.bases.append(st.data_ptr())
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.local.device)
