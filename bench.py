@@ -487,7 +487,7 @@ def main():
                     help="'headline', or one leg name (profiling runs); 'all' runs everything")
     ap.add_argument("--no-shard", action="store_true",
                     help="skip the head-sharded legs (N > 1 only)")
-    ap.add_argument("--peer-stores", type=int, default=0,
+    ap.add_argument("--peer-stores", type=int, default=1,
                     help="N > 1: also time the head-sharded prefill whose kernel stores its rows "
                          "into every rank's output (1) or not (0)")
     ap.add_argument("--prefill-seq", type=int, default=SEQ,
