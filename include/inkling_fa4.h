@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define IFA4_ABI_VERSION 6
+#define IFA4_ABI_VERSION 7
 
 enum {
   IFA4_OK = 0,
@@ -114,15 +114,42 @@ typedef struct IFA4PrefillParams {
    * stream order) and keeps them from reading while a later call overwrites the buffers. */
   const void* const* out_peers;
   int32_t n_out_peers;
+  /* KV split (ABI version 7; not in the reference).  With ifa4_prefill_launch_ws, 0 lets the
+   * library split each query tile's KV tiles over up to IFA4_MAX_KV_SPLITS CTAs when the grid
+   * would leave SMs idle (small batches, few heads), with a merge kernel combining the partials;
+   * a value > 1 forces that many splits; 1 never splits.  ifa4_prefill_launch accepts only 0 or 1
+   * (it has no workspace and never splits). */
+  int32_t kv_splits;
+  /* Longest key sequence, a hint (ABI version 7; <= 0: unknown).  Only the automatic KV-split
+   * choice of ifa4_prefill_launch_ws reads it (the same value gives the same choice whatever the
+   * K/V layout); correctness never depends on it. */
+  int32_t max_seqlen_k;
 } IFA4PrefillParams;
 
 #define IFA4_MAX_OUT_PEERS 7
+#define IFA4_MAX_KV_SPLITS 16
 
 /* Prefill.  Replaces the per-sequence launch loop of inkling_fa4_rel_attention_triton
  * (src/inkling_fa4/triton_kernel.py:84-106) and of the KV-pruned variant
  * (src/inkling_fa4/triton_kernel_kv_pruned.py:210-279): one launch covers all sequences,
  * cu_seqlens are read on the device, and masked KV tiles are never loaded. */
 int ifa4_prefill_launch(const IFA4PrefillParams* params, void* stream);
+
+/* Bytes of device workspace ifa4_prefill_launch_ws needs for these parameters (0 when the launch
+ * does not split the KV range).  No counterpart in the reference, whose prefill launches one
+ * Triton grid per sequence (triton_kernel.py:94-106); it sizes the caller-owned workspace. */
+int ifa4_prefill_workspace_size(const IFA4PrefillParams* params, size_t* bytes_out);
+
+/* Prefill with a caller workspace, which lets small launches (a grid smaller than the GPU: few
+ * sequences, few heads) split each query tile's KV range over several CTAs: each writes a
+ * normalised fp32 partial and its log-sum-exp into the workspace ([splits, total_q, n_heads,
+ * 128] then [splits, n_heads, total_q] floats) and a merge kernel writes out (and lse).  Same
+ * parameters and results as ifa4_prefill_launch (within rounding: the partials are merged in
+ * fp32).  Replaces, like ifa4_prefill_launch, the launch loop of inkling_fa4_rel_attention_triton
+ * (src/inkling_fa4/triton_kernel.py:94-106).  The workspace must be 16-byte aligned and hold
+ * ifa4_prefill_workspace_size bytes; it may be NULL when that size is 0. */
+int ifa4_prefill_launch_ws(const IFA4PrefillParams* params, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Single-token decode (one query per sequence: q [batch, n_heads, head_dim], cu_seqlens_q
  * gives each query's row).  Split-KV: each sequence's visible key range is cut into chunks

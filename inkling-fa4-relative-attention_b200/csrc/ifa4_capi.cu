@@ -308,8 +308,11 @@ const char* ifa4_prefill_tile_config_name(int32_t tile_config) {
   return names[tile_config];
 }
 
-int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
-  g_last_error[0] = '\0';
+}  // extern "C"
+
+namespace {
+int prefill_launch_impl(const IFA4PrefillParams* p, void* workspace, size_t workspace_bytes,
+                        bool ws_entry, size_t* ws_bytes_out, void* stream) {
   int rc = validate_common(p, "prefill");
   if (rc) return rc;
   if (ifa4::prefill_emulated_exp_columns(p->tile_config) < 0)
@@ -317,9 +320,18 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   if (p->block_table != nullptr && !ifa4::prefill_paged_tile_config_ok(p->tile_config))
     return fail(IFA4_ERR_UNSUPPORTED, "prefill: tile_config %d has no paged-cache variant (0 to 3)",
                 p->tile_config);
+  if (p->kv_splits < 0 || p->kv_splits > IFA4_MAX_KV_SPLITS)
+    return fail(IFA4_ERR_INVALID_ARGUMENT, "prefill: kv_splits %d outside [0, %d]", p->kv_splits,
+                IFA4_MAX_KV_SPLITS);
+  if (!ws_entry && p->kv_splits > 1)
+    return fail(IFA4_ERR_INVALID_ARGUMENT,
+                "prefill: kv_splits > 1 needs a workspace (ifa4_prefill_launch_ws)");
+  if (p->kv_splits > 1 && (p->tile_config != 0 || p->n_out_peers > 0))
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: kv_splits > 1 needs tile_config 0 and no out_peers");
+  if (ws_bytes_out) *ws_bytes_out = 0;
   if (p->batch == 0 || p->total_q == 0) return IFA4_OK;
   int* status = nullptr;
-  if ((rc = device_status_ptr(&status))) return rc;
+  if (!ws_bytes_out && (rc = device_status_ptr(&status))) return rc;
 
   ifa4::PrefillKernelArgs a{};
   a.rel = static_cast<const uint16_t*>(p->rel);
@@ -369,11 +381,6 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
                           static_cast<intptr_t>(sizeof(uint16_t));
   }
 
-  CUtensorMap tq, tk, tv;
-  if ((rc = encode_rows_heads_dims(&tq, p->q, p->total_q, p->n_heads, p->q_stride_t,
-                                   p->q_stride_h, 128, "q")))
-    return rc;
-  if ((rc = encode_kv(p, 128, &tk, &tv))) return rc;
   // Grid order: query slots fastest when one query tile's key range over all KV heads (K and V,
   // 512 bytes per key and head; the average sequence's keys, capped by the window) is more than
   // a third of the 126 MB L2 (measured at 32k: causal +1 %, chunked 8 x 18k +8 %; window 4096
@@ -407,12 +414,91 @@ int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
   }
   if (slots < 1) slots = 1;
   if (slots > 65535) slots = 65535;
+  // KV split (workspace entry point only): when the grid leaves SMs idle, each query tile's KV
+  // tiles are shared among kv_splits CTAs and a merge kernel combines their partials.  Measured
+  // on B200 (one sequence, Hq = Hkv = 4 at 2k / 4k / 8k tokens and GQA 8/2 at 4k; 1..16 splits):
+  // a grid of more than half the SMs gains only from 2 splits (8k: 182 -> 167 us; GQA 8/2 at 4k:
+  // 78 -> 77 us, 91 us with 3), a smaller one is best near two waves of CTAs (4k: 113 -> 85 us
+  // with 5; 2k: 84 -> 50 us with 8), with at least 2 KV tiles per share of the heaviest query
+  // tile, which sees at most the longest sequence's keys (the max_seqlen_k hint, else all keys;
+  // the window bounds it).
+  int kv_splits = p->kv_splits > 1 ? p->kv_splits : 1;
+  if (ws_entry && p->kv_splits == 0 && p->tile_config == 0 && p->n_out_peers == 0) {
+    int sms = 148;
+    if ((rc = sm_count(&sms))) return rc;
+    const int64_t head_slots = a.pair_heads ? p->n_heads / 2 : p->n_heads;
+    const int64_t ctas = head_slots * p->batch * slots;
+    int64_t span = p->max_seqlen_k > 0 ? p->max_seqlen_k
+                   : p->block_table != nullptr ? static_cast<int64_t>(p->num_pages) * p->page_size
+                                               : p->total_k;
+    if (p->window_left >= 0 && p->window_left + 256 < span) span = p->window_left + 256;
+    const int64_t kv_tiles = (span + 127) / 128;
+    if (ctas < sms) {
+      int64_t want = 2 * ctas > sms ? 2 : (2 * sms + ctas - 1) / ctas;
+      if (want > kv_tiles / 2) want = kv_tiles / 2;
+      if (want > IFA4_MAX_KV_SPLITS) want = IFA4_MAX_KV_SPLITS;
+      if (want >= 2) kv_splits = static_cast<int>(want);
+    }
+  }
+  if (static_cast<int64_t>(slots) * kv_splits > 65535)
+    return fail(IFA4_ERR_UNSUPPORTED, "prefill: %lld query slots x %d KV splits exceed the grid",
+                static_cast<long long>(slots), kv_splits);
+  const size_t ws_need = kv_splits > 1 ? static_cast<size_t>(kv_splits) * p->total_q *
+                                             p->n_heads * (128 + 1) * sizeof(float)
+                                       : 0;
+  if (ws_bytes_out) {  // planning only
+    *ws_bytes_out = ws_need;
+    return IFA4_OK;
+  }
+  if (ws_need > 0) {
+    if (workspace == nullptr || workspace_bytes < ws_need)
+      return fail(IFA4_ERR_WORKSPACE, "prefill: workspace of %zu bytes required, got %zu", ws_need,
+                  workspace_bytes);
+    if (!aligned16(workspace)) return fail(IFA4_ERR_WORKSPACE, "prefill: workspace must be 16-byte aligned");
+  }
+  a.kv_splits = kv_splits;
+  a.total_q = p->total_q;
+  if (kv_splits > 1) {
+    a.ws_o = static_cast<float*>(workspace);
+    a.ws_lse = a.ws_o + static_cast<size_t>(kv_splits) * p->total_q * p->n_heads * 128;
+  }
+  CUtensorMap tq, tk, tv;
+  if ((rc = encode_rows_heads_dims(&tq, p->q, p->total_q, p->n_heads, p->q_stride_t,
+                                   p->q_stride_h, 128, "q")))
+    return rc;
+  if ((rc = encode_kv(p, 128, &tk, &tv))) return rc;
   cudaError_t e = ifa4::launch_prefill_sm100(a, tq, tk, tv, static_cast<int>(slots),
                                              p->tile_config, static_cast<int>(max_sq),
                                              static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  if (kv_splits > 1) {
+    e = ifa4::launch_prefill_combine_sm100(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "prefill combine launch");
+  }
   return IFA4_OK;
 }
+}  // namespace
+
+extern "C" {
+
+int ifa4_prefill_launch(const IFA4PrefillParams* p, void* stream) {
+  g_last_error[0] = '\0';
+  return prefill_launch_impl(p, nullptr, 0, false, nullptr, stream);
+}
+
+int ifa4_prefill_workspace_size(const IFA4PrefillParams* p, size_t* bytes_out) {
+  g_last_error[0] = '\0';
+  if (bytes_out == nullptr) return fail(IFA4_ERR_INVALID_ARGUMENT, "prefill: bytes_out is NULL");
+  return prefill_launch_impl(p, nullptr, 0, true, bytes_out, nullptr);
+}
+
+int ifa4_prefill_launch_ws(const IFA4PrefillParams* p, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  g_last_error[0] = '\0';
+  return prefill_launch_impl(p, workspace, workspace_bytes, true, nullptr, stream);
+}
+
+
 
 static int decode_plan(const IFA4DecodeParams* p, int* num_splits, int* chunk_len,
                        size_t* ws_bytes) {

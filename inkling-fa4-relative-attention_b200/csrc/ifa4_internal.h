@@ -67,6 +67,13 @@ struct PrefillKernelArgs {
   // output copies on other GPUs: element e of out is also stored at out + out_peer_delta[i] + e
   long long out_peer_delta[7];
   int n_out_peers;
+  // KV split (kv_splits > 1): the query tile's KV tiles are cut into kv_splits ranges, one per
+  // CTA; each writes its rows' normalised fp32 partial output and log2-sum-exp, and
+  // rel_attn_prefill_combine_kernel merges them into out (and lse)
+  int kv_splits;
+  float* ws_o;               // [kv_splits, total_q, n_heads, 128]
+  float* ws_lse;             // [kv_splits, n_heads, total_q], log2 units, -inf: no visible key
+  long long total_q;
 };
 
 struct PrefillLaunch {
@@ -89,6 +96,8 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
                                  const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                  int q_slots, int tile_config, int max_seqlen_q,
                                  cudaStream_t stream);
+// Merge of the kv_splits partials written by a split launch (one warp per token and head).
+cudaError_t launch_prefill_combine_sm100(const PrefillKernelArgs& args, cudaStream_t stream);
 bool prefill_paged_tile_config_ok(int tile_config);
 
 struct DecodeKernelArgs {

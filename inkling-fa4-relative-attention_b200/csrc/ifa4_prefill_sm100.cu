@@ -91,7 +91,7 @@ struct TileInfo {
 };
 
 __device__ __forceinline__ TileInfo tile_info(const PrefillKernelArgs& a, int qt, int hslot,
-                                              int sq, int sk) {
+                                              int sq, int sk, bool split_on, int split) {
   TileInfo t;
   if (a.pair_heads) {
     t.head[0] = 2 * hslot;
@@ -126,16 +126,23 @@ __device__ __forceinline__ TileInfo tile_info(const PrefillKernelArgs& a, int qt
     t.j_lo = lo / kBN;
     t.n_kv = (hi + kBN - 1) / kBN - t.j_lo;
   }
+  if (split_on && t.n_kv > 0) {  // this CTA's share of the KV tiles: [first, first + n)
+    const int per = (t.n_kv + a.kv_splits - 1) / a.kv_splits;
+    const int first = split * per;
+    t.j_lo += first;
+    t.n_kv = max(0, min(per, t.n_kv - first));
+  }
   return t;
 }
 
 // Producer for a paged KV cache: run by all 32 lanes of warp 0 (see the file comment).
+template <bool kSplit>
 __device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_t* smem,
                                               Bars* bars, const CUtensorMap* tm_q,
                                               const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                               int hslot, int b, int q_start, int sq, int sk,
-                                              int n_qt, int slot0, int slot_step, int lane,
-                                              const AbortCtx& ab) {
+                                              int n_qt, int slot0, int slot_step, int split,
+                                              int lane, const AbortCtx& ab) {
   uint32_t qc = 0, kc = 0, vc = 0;
   const uint64_t pol_kv = l2_policy_evict_last();
   const uint64_t pol_q = l2_policy_evict_first();
@@ -145,7 +152,7 @@ __device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_
   const int32_t* bt = a.block_table + static_cast<long long>(b) * a.bt_stride;
   bool ok = true;
   for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
-    const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+    const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk, kSplit, split);
     if (t.n_kv == 0) continue;
     if (!(ok = mbar_wait_warp(&bars->q_empty, (qc & 1) ^ 1, ab))) break;
     if (lane == 0) {
@@ -259,7 +266,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint3
   }
 }
 
-template <int kEmu, int kHalf2, bool kPaged, bool kPeers>
+template <int kEmu, int kHalf2, bool kPaged, bool kPeers, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     rel_attn_prefill_kernel(const __grid_constant__ PrefillKernelArgs a,
                             const __grid_constant__ CUtensorMap tm_q,
@@ -277,10 +284,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   // resident at one time read the K/V of few KV heads and those tiles stay in L2.  Otherwise
   // (head slots, sequences, query slots), which spreads a ragged batch's sequences over the
   // first waves.
+  // The slot dimension carries the query slot and, for a split launch, the KV split (fastest).
   const int hslot = a.q_fastest ? blockIdx.y : blockIdx.x;
   const int b = a.q_fastest ? blockIdx.z : blockIdx.y;
-  const int slot0 = a.q_fastest ? blockIdx.x : blockIdx.z;
-  const int slot_step = a.q_fastest ? gridDim.x : gridDim.z;
+  const int slot_idx = a.q_fastest ? blockIdx.x : blockIdx.z;
+  const int nsplit = kSplit ? a.kv_splits : 1;
+  const int split = slot_idx % nsplit;
+  const int slot0 = slot_idx / nsplit;
+  const int slot_step = (a.q_fastest ? gridDim.x : gridDim.z) / nsplit;
   const int q_start = a.cu_q[b];
   const int sq = a.cu_q[b + 1] - q_start;
   const int k_start = a.cu_k[b];
@@ -322,8 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
   if (warp < 4) {
    if (kPaged && warp == 0) {
-    produce_paged(a, smem, bars, &tm_q, &tm_k, &tm_v, hslot, b, q_start, sq, sk, n_qt, slot0,
-                  slot_step, lane, ab);
+    produce_paged<kSplit>(a, smem, bars, &tm_q, &tm_k, &tm_v, hslot, b, q_start, sq, sk, n_qt,
+                          slot0, slot_step, split, lane, ab);
    } else if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -331,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_kv = l2_policy_evict_last();
       const uint64_t pol_q = l2_policy_evict_first();
       for (int slot = slot0; slot < n_qt; slot += slot_step) {
-        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk, kSplit, split);
         if (t.n_kv == 0) continue;
         if (!mbar_wait(&bars->q_empty, (qc & 1) ^ 1, ab)) break;
         mbar_arrive_expect_tx(&bars->q_full, 2 * kTile);
@@ -383,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t v_addr = smem_u32(smem + kSmemV);
       bool ok = true;
       for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
-        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+        const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk, kSplit, split);
         if (t.n_kv == 0) continue;
         if (!(ok = mbar_wait(&bars->q_full, qc & 1, ab))) break;
         ++qc;
@@ -455,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t pc = 0, oc = 0;
     bool ok = true;
     for (int slot = slot0; slot < n_qt && ok; slot += slot_step) {
-      const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk);
+      const TileInfo t = tile_info(a, n_qt - 1 - slot, hslot, sq, sk, kSplit, split);
       const int qi = t.row0[s] + row;
       const bool row_valid = qi < sq;
       const int h = t.head[s];
@@ -463,12 +474,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                           static_cast<long long>(h) * a.out_sh;
       if (t.n_kv == 0) {
         if (row_valid) {
-          uint4 z = make_uint4(0, 0, 0, 0);
+          if (kSplit) {  // an empty share: its partial carries no weight in the merge
+            a.ws_lse[(static_cast<long long>(split) * a.n_heads + h) * a.total_q + q_start + qi] =
+                -INFINITY;
+          } else {
+            uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) reinterpret_cast<uint4*>(out_row)[c] = z;
-          if (a.lse != nullptr)
-            a.lse[static_cast<long long>(h) * a.lse_sh +
-                  static_cast<long long>(q_start + qi) * a.lse_st] = -INFINITY;
+            for (int c = 0; c < 16; ++c) reinterpret_cast<uint4*>(out_row)[c] = z;
+            if (a.lse != nullptr)
+              a.lse[static_cast<long long>(h) * a.lse_sh +
+                    static_cast<long long>(q_start + qi) * a.lse_st] = -INFINITY;
+          }
         }
         continue;
       }
@@ -739,10 +755,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       // a row that never saw a visible key outputs 0 (its running max is still -inf)
       const bool seen = l_run > 0.f && m_run != -INFINITY;
       const float inv_l = seen ? 1.f / l_run : 0.f;
-      if (a.lse != nullptr && row_valid)  // ln(sum exp) = ln2 * (m + log2 l) in the exp2 domain
+      if (!kSplit && a.lse != nullptr && row_valid)  // ln(sum exp) = ln2 (m + log2 l)
         a.lse[static_cast<long long>(h) * a.lse_sh + static_cast<long long>(q_start + qi) * a.lse_st] =
             seen ? (m_run + __log2f(l_run)) * 0.6931471805599453f : -INFINITY;
       uint8_t* stage = smem + kSmemQ + s * kTile;
+      if (kSplit) {
+        // normalised fp32 partial (two 64-column halves, each staged through the Q buffer as
+        // whole 256-byte row segments) and its log2-sum-exp, for the merge kernel
+        if (row_valid)
+          a.ws_lse[(static_cast<long long>(split) * a.n_heads + h) * a.total_q + q_start + qi] =
+              seen ? m_run + __log2f(l_run) : -INFINITY;
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp) {
+          __syncwarp();  // the previous half's reads of the stage are done
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + hp * 64 + c * 32, o);
+            tmem_wait_ld();
+            if (hp == 1 && c == 1) {  // TMEM O may be overwritten by the next work tile
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars->o_empty[s]);
+            }
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const int g = c * 8 + v;  // 16-byte granule (4 floats) of the 256-byte segment
+              uint4* dst = reinterpret_cast<uint4*>(stage + (g >> 3) * kHalf + row * 128 +
+                                                    (((g & 7) ^ (row & 7)) << 4));
+              *dst = make_uint4(__float_as_uint(__uint_as_float(o[4 * v]) * inv_l),
+                                __float_as_uint(__uint_as_float(o[4 * v + 1]) * inv_l),
+                                __float_as_uint(__uint_as_float(o[4 * v + 2]) * inv_l),
+                                __float_as_uint(__uint_as_float(o[4 * v + 3]) * inv_l));
+            }
+          }
+          __syncwarp();
+          const int wrow0 = (warp & 3) * 32;
+          const int g = lane & 15;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int r = wrow0 + 2 * i + (lane >> 4);
+            const uint4 val = *reinterpret_cast<const uint4*>(
+                stage + (g >> 3) * kHalf + r * 128 + (((g & 7) ^ (r & 7)) << 4));
+            const int qr = t.row0[s] + r;
+            if (qr < sq)
+              *reinterpret_cast<uint4*>(
+                  a.ws_o + ((static_cast<long long>(split) * a.total_q + q_start + qr) * a.n_heads +
+                            h) * 128 + hp * 64 + g * 4) = val;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->q_empty);
+        continue;
+      }
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -803,19 +868,59 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Merge of a split launch's partials, one warp per (token, head): weights 2^(lse_s - max lse)
+// over the splits that saw a key; lanes own 4 of the 128 dims (16-byte loads, 8-byte stores).
+__global__ void __launch_bounds__(256)
+    rel_attn_prefill_combine_kernel(const __grid_constant__ PrefillKernelArgs a) {
+  const long long w = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= a.total_q * a.n_heads) return;
+  const long long t = w / a.n_heads;
+  const int h = static_cast<int>(w % a.n_heads);
+  const int S = a.kv_splits;
+  float M = -INFINITY;
+  for (int sp = 0; sp < S; ++sp)
+    M = fmaxf(M, a.ws_lse[(static_cast<long long>(sp) * a.n_heads + h) * a.total_q + t]);
+  float wsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY) {
+    for (int sp = 0; sp < S; ++sp) {
+      const float l = a.ws_lse[(static_cast<long long>(sp) * a.n_heads + h) * a.total_q + t];
+      if (l == -INFINITY) continue;  // an empty share (its partial was never written)
+      const float wt = fast_exp2(l - M);
+      const float4 o = reinterpret_cast<const float4*>(
+          a.ws_o + ((static_cast<long long>(sp) * a.total_q + t) * a.n_heads + h) * 128)[lane];
+      wsum += wt;
+      acc.x += wt * o.x;
+      acc.y += wt * o.y;
+      acc.z += wt * o.z;
+      acc.w += wt * o.w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  uint2 packed;
+  packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(a.out + t * a.out_st + static_cast<long long>(h) * a.out_sh +
+                            lane * 4) = packed;
+  if (lane == 0 && a.lse != nullptr)  // log2-sum-exp of the partials -> natural log
+    a.lse[static_cast<long long>(h) * a.lse_sh + t * a.lse_st] =
+        wsum > 0.f ? (M + __log2f(wsum)) * 0.6931471805599453f : -INFINITY;
+}
+
 }  // namespace prefill
 
 namespace {
-template <int kEmu, int kHalf2, bool kPaged, bool kPeers = false>
+template <int kEmu, int kHalf2, bool kPaged, bool kPeers = false, bool kSplit = false>
 cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_q,
                            const CUtensorMap& tm_k, const CUtensorMap& tm_v, dim3 grid,
                            cudaStream_t stream) {
   static std::atomic<bool> attr_set[64];
   cudaError_t e =
-      set_smem_limit_once(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kPeers>,
+      set_smem_limit_once(prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kPeers, kSplit>,
                           prefill::kSmemAlloc, attr_set);
   if (e != cudaSuccess) return e;
-  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kPeers>
+  prefill::rel_attn_prefill_kernel<kEmu, kHalf2, kPaged, kPeers, kSplit>
       <<<grid, prefill::kThreads, prefill::kSmemAlloc, stream>>>(args, tm_q, tm_k, tm_v);
   return cudaGetLastError();
 }
@@ -825,6 +930,15 @@ cudaError_t launch_variant(const PrefillKernelArgs& args, const CUtensorMap& tm_
 static const int kVariants[kPrefillNumTileConfigs][2] = {
     {kPrefillDefaultEmu, kPrefillDefaultHalf2}, {0, 0}, {2, 0}, {4, 0}, {6, 0}, {8, 0},
     {0, 16}, {0, 8}, {4, 8}};
+
+cudaError_t launch_prefill_combine_sm100(const PrefillKernelArgs& args, cudaStream_t stream) {
+  const long long pairs = args.total_q * args.n_heads;
+  const long long blocks = (pairs + 7) / 8;
+  if (blocks <= 0) return cudaSuccess;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  prefill::rel_attn_prefill_combine_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(args);
+  return cudaGetLastError();
+}
 
 bool prefill_paged_tile_config_ok(int tile_config) {
   return tile_config >= 0 && tile_config <= 3;
@@ -851,6 +965,14 @@ cudaError_t launch_prefill_sm100(const PrefillKernelArgs& args, const CUtensorMa
     // lose 4 % at 32k.
     emu = 2;
     h2 = 0;
+  }
+  if (args.kv_splits > 1) {  // KV split: the automatic choice, contiguous or paged K/V
+    if (args.n_out_peers > 0 || emu != 2 || h2 != 0) return cudaErrorInvalidValue;
+    grid = args.q_fastest ? dim3(q_slots * args.kv_splits, head_slots, args.batch)
+                          : dim3(head_slots, args.batch, q_slots * args.kv_splits);
+    if (args.block_table != nullptr)
+      return launch_variant<2, 0, true, false, true>(args, tm_q, tm_k, tm_v, grid, stream);
+    return launch_variant<2, 0, false, false, true>(args, tm_q, tm_k, tm_v, grid, stream);
   }
   if (args.n_out_peers > 0) {  // output copies on other GPUs: contiguous K/V, automatic choice
     if (args.block_table != nullptr || emu != 2 || h2 != 0) return cudaErrorInvalidValue;

@@ -19,12 +19,15 @@ IFA4_ERR_DEVICE_TIMEOUT = -5
 IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0
-ABI_VERSION = 6
+ABI_VERSION = 7
 MAX_OUT_PEERS = 7
+MAX_KV_SPLITS = 16
 NOALLOC_DECODE_SCRATCH_BYTES = 16 * 1024 * 1024
 
 EXPORTED_SYMBOLS = (
     "ifa4_prefill_launch",
+    "ifa4_prefill_launch_ws",
+    "ifa4_prefill_workspace_size",
     "ifa4_decode_launch",
     "ifa4_decode_launch_noalloc",
     "ifa4_decode_workspace_size",
@@ -65,6 +68,7 @@ class PrefillParams(ctypes.Structure):
         ("k_stride_page", ctypes.c_int64), ("v_stride_page", ctypes.c_int64),
         ("page_size", ctypes.c_int32), ("num_pages", ctypes.c_int32),
         ("out_peers", ctypes.POINTER(ctypes.c_void_p)), ("n_out_peers", ctypes.c_int32),
+        ("kv_splits", ctypes.c_int32), ("max_seqlen_k", ctypes.c_int32),
     ]
 
 
@@ -134,6 +138,10 @@ def lib() -> ctypes.CDLL:
     vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
     L.ifa4_prefill_launch.argtypes = [ctypes.POINTER(PrefillParams), vp]
     L.ifa4_prefill_launch.restype = ctypes.c_int
+    L.ifa4_prefill_launch_ws.argtypes = [ctypes.POINTER(PrefillParams), vp, sz, vp]
+    L.ifa4_prefill_launch_ws.restype = ctypes.c_int
+    L.ifa4_prefill_workspace_size.argtypes = [ctypes.POINTER(PrefillParams), ctypes.POINTER(sz)]
+    L.ifa4_prefill_workspace_size.restype = ctypes.c_int
     L.ifa4_decode_launch.argtypes = [ctypes.POINTER(DecodeParams), vp, sz, vp]
     L.ifa4_decode_launch.restype = ctypes.c_int
     L.ifa4_decode_launch_noalloc.argtypes = [ctypes.POINTER(DecodeParams), vp]

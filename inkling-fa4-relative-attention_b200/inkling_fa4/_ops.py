@@ -171,10 +171,14 @@ def _table(block_table):
 def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
             rel_extent, causal=True, window_size=(-1, -1), n_heads=None, kv_heads=None,
             head_dim=HEAD_DIM, softmax_scale=None, causal_align="reference", out=None,
-            tile_config=0, return_lse=False, lse=None, block_table=None, out_peers=None):
+            tile_config=0, return_lse=False, lse=None, block_table=None, out_peers=None,
+            kv_splits=0, workspace=None):
     """``out_peers``: optional device addresses (valid in this process) of the element that
     corresponds to ``out[0, 0, 0]`` in other GPUs' output buffers laid out like ``out``'s; the
-    kernel stores every output row there too (see ``inkling_fa4.sharding.PeerOutputs``)."""
+    kernel stores every output row there too (see ``inkling_fa4.sharding.PeerOutputs``).
+    ``kv_splits``: 0 lets the library split each query tile's KV range over several CTAs when
+    the launch is too small to fill the GPU (the partials go to ``workspace``, allocated here if
+    not given or too small); 1 never splits; > 1 forces that many splits."""
     block_table = _table(block_table)
     q, k, v, rel, out, n_heads, kv_heads, rel_extent, window_left, scale = _prepare(
         "prefill", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
@@ -187,6 +191,8 @@ def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_s
     p.max_seqlen_q = int(max_seqlen_q) if max_seqlen_q else 0
     p.softmax_scale = scale
     p.tile_config = int(tile_config)
+    p.kv_splits = int(kv_splits)
+    p.max_seqlen_k = int(max_seqlen_k) if max_seqlen_k else 0
     peers = None
     if out_peers:
         if len(out_peers) > _lib.MAX_OUT_PEERS:
@@ -194,9 +200,21 @@ def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_s
         peers = (ctypes.c_void_p * len(out_peers))(*[int(x) for x in out_peers])
         p.out_peers = ctypes.cast(peers, ctypes.POINTER(ctypes.c_void_p))
         p.n_out_peers = len(out_peers)
+    L = _lib.lib()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        _lib.check(_lib.lib().ifa4_prefill_launch(ctypes.byref(p), ctypes.c_void_p(stream)))
+        if p.kv_splits == 1 or p.n_out_peers > 0:
+            _lib.check(L.ifa4_prefill_launch(ctypes.byref(p), ctypes.c_void_p(stream)))
+        else:
+            nbytes = ctypes.c_size_t(0)
+            _lib.check(L.ifa4_prefill_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)))
+            need = int(nbytes.value)
+            if need > 0 and (workspace is None
+                             or workspace.numel() * workspace.element_size() < need):
+                workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            ws_ptr = workspace.data_ptr() if need > 0 else 0
+            _lib.check(L.ifa4_prefill_launch_ws(ctypes.byref(p), ctypes.c_void_p(ws_ptr),
+                                                ctypes.c_size_t(need), ctypes.c_void_p(stream)))
     return (out, lse) if lse is not None else out
 
 

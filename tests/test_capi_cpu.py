@@ -206,3 +206,41 @@ def test_read_stream_hook_validates_before_any_cuda_call():
     # misaligned size, with non-null (never dereferenced) pointers
     assert L.ifa4_measure_read_stream(16, 24, 16, None) == _lib.IFA4_ERR_INVALID_ARGUMENT
     assert b"16-byte" in L.ifa4_last_error_string()
+
+
+def _valid_prefill(**kw):
+    base = dict(q=256, k=256, v=256, rel=256, out=256, cu_seqlens_q=256, cu_seqlens_k=256,
+                q_stride_t=512, q_stride_h=128, k_stride_t=512, k_stride_h=128, v_stride_t=512,
+                v_stride_h=128, rel_stride_t=512, rel_stride_h=128, out_stride_t=512,
+                out_stride_h=128)
+    base.update(kw)
+    return _params(**base)
+
+
+@pytest.mark.parametrize("kw,entry,code", [
+    (dict(kv_splits=2), "launch", _lib.IFA4_ERR_INVALID_ARGUMENT),  # a split needs a workspace
+    (dict(kv_splits=-1), "ws", _lib.IFA4_ERR_INVALID_ARGUMENT),
+    (dict(kv_splits=_lib.MAX_KV_SPLITS + 1), "ws", _lib.IFA4_ERR_INVALID_ARGUMENT),
+    (dict(kv_splits=2, tile_config=1), "ws", _lib.IFA4_ERR_UNSUPPORTED),
+])
+def test_prefill_kv_split_validation_before_any_cuda_call(kw, entry, code):
+    L = _lib.lib()
+    p = _valid_prefill(**kw)
+    if entry == "launch":
+        rc = L.ifa4_prefill_launch(ctypes.byref(p), None)
+    else:
+        rc = L.ifa4_prefill_launch_ws(ctypes.byref(p), None, 0, None)
+        nbytes = ctypes.c_size_t(123)
+        assert L.ifa4_prefill_workspace_size(ctypes.byref(p), ctypes.byref(nbytes)) == code
+    assert rc == code
+    assert b"kv_splits" in L.ifa4_last_error_string()
+
+
+def test_prefill_workspace_size_of_an_empty_batch_is_zero():
+    L = _lib.lib()
+    nbytes = ctypes.c_size_t(123)
+    assert L.ifa4_prefill_workspace_size(ctypes.byref(_valid_prefill(batch=0)),
+                                         ctypes.byref(nbytes)) == _lib.IFA4_OK
+    assert nbytes.value == 0
+    assert L.ifa4_prefill_workspace_size(ctypes.byref(_valid_prefill()), None) == \
+        _lib.IFA4_ERR_INVALID_ARGUMENT
