@@ -343,7 +343,8 @@ int ifa4_measure_read_stream(const void* buf, size_t bytes, uint32_t* sink, void
 /* Reads (and optionally clears) the library's device status word on `stream`, blocking the
  * calling thread until the stream has reached this point.  Nonzero means a kernel gave up on
  * a bounded wait (a bug, never expected): bit 0 prefill, bit 1 decode, bit 2 backward, bits 3-4
- * ifa4_selftest_bounded_wait, bit 5 rel_logits producer.  Test hook; the
+ * ifa4_selftest_bounded_wait, bit 5 rel_logits producer, bit 6 (debug builds compiled with
+ * -DIFA4_DEBUG only) an index range check failed and the access was skipped.  Test hook; the
  * reference has no counterpart. */
 int ifa4_read_device_status(void* stream, int32_t clear, int32_t* status_out);
 

@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const KeyBlock blk = key_block(a, k0, sq, sk);
       const int kl = k0 + r;  // this thread's key (local to the sequence)
       const bool key_valid = kl < sk;
+      IFA4_DBG_CHECK(a.status, !key_valid || k_start + kl < a.total_k);  // report only
       uint16_t* dk_row = a.dk + static_cast<long long>(k_start + kl) * a.dk_st +
                          static_cast<long long>(kvh) * a.dk_sh + half * 64;
       uint16_t* dv_row = a.dv + static_cast<long long>(k_start + kl) * a.dv_st +
@@ -790,6 +791,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const QTile t = q_tile(a, q0, sq, sk);
       const int qi = q0 + r;
       const bool row_valid = qi < sq;
+      IFA4_DBG_CHECK(a.status, !row_valid || q_start + qi < a.total_q);  // report only
       uint16_t* dq_row = a.dq + static_cast<long long>(q_start + qi) * a.dq_st +
                          static_cast<long long>(h) * a.dq_sh + half * 64;
       if (t.n_kv == 0) {

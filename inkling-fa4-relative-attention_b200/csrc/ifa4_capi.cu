@@ -804,6 +804,7 @@ int ifa4_backward_launch(const IFA4BackwardParams* p, void* workspace, size_t wo
   a.drel_st = p->drel_stride_t;
   a.drel_sh = p->drel_stride_h;
   a.total_q = p->total_q;
+  a.total_k = p->total_k;
   a.batch = p->batch;
   a.n_heads = p->n_heads;
   a.kv_heads = p->kv_heads;

@@ -419,7 +419,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const int h = h0 + row;
       const float val = L > 0.f ? acc / L : 0.f;
-      if (gridDim.x == 1) {
+      if (!IFA4_DBG_CHECK(a.status, si.q_row >= 0 && si.q_row < a.batch && h < a.n_heads)) {
+        // a bad query row or head: nothing is stored
+      } else if (gridDim.x == 1) {
         uint16_t* dst = a.out + static_cast<long long>(si.q_row) * a.out_st +
                         static_cast<long long>(h) * a.out_sh + d;
         __nv_bfloat16 bv = __float2bfloat16_rn(val);
@@ -442,6 +444,7 @@ __global__ void __launch_bounds__(128)
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int S = a.num_splits;
   const long long base = (static_cast<long long>(b) * a.n_heads + h) * S;
+  if (!IFA4_DBG_CHECK(a.status, a.cu_q[b] >= 0 && a.cu_q[b] < a.batch)) return;
   float M = -INFINITY;
   for (int s = 0; s < S; ++s) M = fmaxf(M, a.ws_lse[base + s]);
   float wsum = 0.f, acc = 0.f;

@@ -37,6 +37,21 @@ constexpr int kStatusBackwardTimeout = 4;
 constexpr int kStatusSelfTestTimeout = 8;   // ifa4_selftest_bounded_wait, warp 0
 constexpr int kStatusSelfTestOwnTimeout = 16;  // ifa4_selftest_bounded_wait, warp 1 (must not be set)
 constexpr int kStatusRelLogitsTimeout = 32;
+constexpr int kStatusDebugBounds = 64;   // debug builds only: an index range check failed
+
+// Index range checks of debug builds (compiled with -DIFA4_DEBUG, the library's stand-in for a
+// bounds-checking sanitizer): a failed check ORs kStatusDebugBounds into the status word and the
+// guarded access is skipped, so a bad index is reported without touching memory out of range.
+// In release builds the condition is not evaluated and the access is unconditional.
+#ifdef IFA4_DEBUG
+__device__ __forceinline__ bool debug_check(int* status, bool ok) {
+  if (!ok && status != nullptr) atomicOr(status, kStatusDebugBounds);
+  return ok;
+}
+#define IFA4_DBG_CHECK(status, cond) ::ifa4::debug_check((status), (cond))
+#else
+#define IFA4_DBG_CHECK(status, cond) true
+#endif
 
 struct PrefillKernelArgs {
   const uint16_t* rel;       // bf16 bits
@@ -135,6 +150,7 @@ struct BackwardKernelArgs {
   const uint16_t* dout;      // incoming gradient dO
   const float* lse;          // forward natural-log LSE, [h * lse_sh + token * lse_st]
   float* delta;              // workspace [n_heads, total_q]: rowsum(dO * O)
+  long long total_k;         // rows of k / v / dk / dv (index checks of debug builds)
   uint16_t* dq;
   uint16_t* dk;
   uint16_t* dv;

@@ -201,6 +201,7 @@ __device__ __forceinline__ void produce_paged(const PrefillKernelArgs& a, uint8_
       uint32_t v_bytes = kTile;
       if (pu >= 0) {
         const int pblk = __shfl_sync(0xffffffffu, blk, pu);
+        IFA4_DBG_CHECK(a.status, pblk < a.num_pages);
         const int pkey = key0 + pu * box;
         const int nvalid = sk - pkey;
         const uint16_t* src = a.v + static_cast<long long>(pblk < 0 ? 0 : pblk) * a.v_sp +
@@ -475,9 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t.n_kv == 0) {
         if (row_valid) {
           if (kSplit) {  // an empty share: its partial carries no weight in the merge
-            a.ws_lse[(static_cast<long long>(split) * a.n_heads + h) * a.total_q + q_start + qi] =
+            if (IFA4_DBG_CHECK(a.status, split < a.kv_splits && q_start + qi < a.total_q))
+              a.ws_lse[(static_cast<long long>(split) * a.n_heads + h) * a.total_q + q_start + qi] =
                 -INFINITY;
-          } else {
+          } else if (IFA4_DBG_CHECK(a.status, q_start + qi < a.total_q && h < a.n_heads)) {
             uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
             for (int c = 0; c < 16; ++c) reinterpret_cast<uint4*>(out_row)[c] = z;
@@ -488,6 +490,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
+      // report only (TMA loads outside a tensor read zeros, and rows past the sequence end are
+      // never stored): the visited KV tiles start inside the sequence, the row inside the batch
+      IFA4_DBG_CHECK(a.status, t.j_lo >= 0 && (t.j_lo + t.n_kv - 1) * kBN < sk &&
+                                   (!row_valid || q_start + qi < a.total_q));
       const uint16_t* rel_row = a.rel + static_cast<long long>(q_start + qi) * a.rel_st +
                                 static_cast<long long>(h) * a.rel_sh;
       // visible keys of this row: [key_lo, key_hi)
@@ -755,14 +761,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // a row that never saw a visible key outputs 0 (its running max is still -inf)
       const bool seen = l_run > 0.f && m_run != -INFINITY;
       const float inv_l = seen ? 1.f / l_run : 0.f;
-      if (!kSplit && a.lse != nullptr && row_valid)  // ln(sum exp) = ln2 (m + log2 l)
+      if (!kSplit && a.lse != nullptr && row_valid &&  // ln(sum exp) = ln2 (m + log2 l)
+          IFA4_DBG_CHECK(a.status, q_start + qi < a.total_q && h < a.n_heads))
         a.lse[static_cast<long long>(h) * a.lse_sh + static_cast<long long>(q_start + qi) * a.lse_st] =
             seen ? (m_run + __log2f(l_run)) * 0.6931471805599453f : -INFINITY;
       uint8_t* stage = smem + kSmemQ + s * kTile;
       if (kSplit) {
         // normalised fp32 partial (two 64-column halves, each staged through the Q buffer as
         // whole 256-byte row segments) and its log2-sum-exp, for the merge kernel
-        if (row_valid)
+        if (row_valid && IFA4_DBG_CHECK(a.status, split < a.kv_splits && q_start + qi < a.total_q))
           a.ws_lse[(static_cast<long long>(split) * a.n_heads + h) * a.total_q + q_start + qi] =
               seen ? m_run + __log2f(l_run) : -INFINITY;
 #pragma unroll
@@ -798,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint4 val = *reinterpret_cast<const uint4*>(
                 stage + (g >> 3) * kHalf + r * 128 + (((g & 7) ^ (r & 7)) << 4));
             const int qr = t.row0[s] + r;
-            if (qr < sq)
+            if (qr < sq && IFA4_DBG_CHECK(a.status, q_start + qr < a.total_q))
               *reinterpret_cast<uint4*>(
                   a.ws_o + ((static_cast<long long>(split) * a.total_q + q_start + qr) * a.n_heads +
                             h) * 128 + hp * 64 + g * 4) = val;
@@ -842,7 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4 val = *reinterpret_cast<const uint4*>(
               stage + (g >> 3) * kHalf + r * 128 + (((g & 7) ^ (r & 7)) << 4));
           const int qr = t.row0[s] + r;
-          if (qr < sq) {
+          if (qr < sq && IFA4_DBG_CHECK(a.status, q_start + qr < a.total_q && h < a.n_heads)) {
             uint16_t* dst = a.out + static_cast<long long>(q_start + qr) * a.out_st +
                             static_cast<long long>(h) * a.out_sh + g * 8;
             *reinterpret_cast<uint4*>(dst) = val;
@@ -878,6 +885,8 @@ __global__ void __launch_bounds__(256)
   const long long t = w / a.n_heads;
   const int h = static_cast<int>(w % a.n_heads);
   const int S = a.kv_splits;
+  if (!IFA4_DBG_CHECK(a.status, S >= 2 && S <= 16 && a.ws_o != nullptr && a.ws_lse != nullptr))
+    return;
   float M = -INFINITY;
   for (int sp = 0; sp < S; ++sp)
     M = fmaxf(M, a.ws_lse[(static_cast<long long>(sp) * a.n_heads + h) * a.total_q + t]);

@@ -8,7 +8,10 @@ from __future__ import annotations
 import ctypes
 import os
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libinkling_fa4.so")
+_LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
+# INKLING_FA4_LIB=debug loads the index-checking debug build (python -m inkling_fa4.build --debug)
+LIB_PATH = os.path.join(_LIB_DIR, "libinkling_fa4_debug.so"
+                        if os.environ.get("INKLING_FA4_LIB") == "debug" else "libinkling_fa4.so")
 
 IFA4_OK = 0
 IFA4_ERR_INVALID_ARGUMENT = -1
@@ -16,6 +19,7 @@ IFA4_ERR_UNSUPPORTED = -2
 IFA4_ERR_CUDA = -3
 IFA4_ERR_WORKSPACE = -4
 IFA4_ERR_DEVICE_TIMEOUT = -5
+STATUS_DEBUG_BOUNDS = 64
 IFA4_ALIGN_REFERENCE = 0
 IFA4_ALIGN_BOTTOM_RIGHT = 1
 IFA4_DTYPE_BF16 = 0

@@ -103,10 +103,15 @@ def test_noncontiguous_inputs_and_out_param():
 
 
 def test_max_seqlen_hint_is_not_trusted_for_correctness():
+    """Wrong max_seqlen hints change only the grid shape (and, with the automatic KV split of
+    small launches, the split count, i.e. the rounding of the merge), never the result."""
+    from inkling_fa4 import _ops
     c = to_dev(make_case([600, 40], [600, 40], 4, 2, 128, seed=8))
-    good = run_prefill(c)
-    bad = inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 1, 1, 128)
+    good = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 600, 600, 128, kv_splits=1)
+    bad = _ops.prefill(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 1, 1, 128, kv_splits=1)
     torch.testing.assert_close(bad, good, atol=0, rtol=0)
+    auto_bad = inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, 1, 1, 128)
+    assert_close(np32(auto_bad), oracle_full(c, 1 / 128))
 
 
 def test_empty_keys_give_zero_rows():
