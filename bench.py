@@ -438,6 +438,36 @@ def timed(fn, steps, warmup, stream, dist=None, barrier=None):
     return ms, med
 
 
+def graph_replay_us(fn, calls=10, reps=100):
+    """Device time per call of `fn` replayed from a CUDA graph of `calls` calls (the calls'
+    host-side Python and ctypes work is paid once, at capture), so launch-latency-bound calls
+    show their device time rather than the host's."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(calls):
+            fn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / (reps * calls)
+    del graph
+    return us
+
+
 def read_stream_peak(dev, stream):
     """The read-only HBM stream ceiling of this GPU, measured in the run: the library's
     measurement hook (16-byte non-coherent loads, four in flight per thread) over a 4 GiB
@@ -845,6 +875,11 @@ def main():
                            "softmax_scale": 128 ** -0.5, "rel": "per-head table (token stride 0)",
                            "note": "launch-latency bound: one 128-row tile per head"},
                           softmax_scale=128 ** -0.5)
+        # eager calls of this size are bound by the host (Python + ctypes, about 40 us per call);
+        # replayed from a CUDA graph they show the kernel's own time
+        leg["graph_replay_us_per_call"] = graph_replay_us(
+            lambda: prefill_call(c1.q, c1.k, c1.v, c1.rel, c1.cu_q, c1.cu_k, c1.max_q, c1.max_k,
+                                 c1.rel_extent, softmax_scale=128 ** -0.5))
         result["config1"] = leg
         del c1
 
@@ -1020,6 +1055,7 @@ def main():
         host_us = (time.perf_counter() - t0) / 200 * 1e6
         torch.cuda.synchronize()
         sms, smed = timed(small_step, steps2, warm2, stream)
+        sgraph = graph_replay_us(small_step)
         result["decode"] = {
             "value": gbs, "unit": "GB/s", "us_per_step": us, "us_per_step_median": dmed * 1e3,
             "steps": steps2,
@@ -1033,6 +1069,7 @@ def main():
                              traffic_note="batch-16 ncu capture scaled to batch 128 by K/V bytes"),
             "host_call_overhead_b1": {
                 "host_us_per_call": host_us, "device_us_per_call_median": smed * 1e3,
+                "device_us_per_call_graph_replay": sgraph,
                 "kv_tokens": small.max_k,
                 "note": "wall clock of 200 back-to-back Python calls (argument checks, ctypes "
                         "struct, plan query, 2 launches) vs CUDA-event device time; the host "
