@@ -101,3 +101,22 @@ def test_select_sequences_packs_subset():
     q, rel, k, v, cq, ck = select_sequences([0, 2], c.cu_q, c.cu_k, c.q, c.rel, c.k, c.v)
     assert cq.tolist() == [0, 3, 5] and ck.tolist() == [0, 4, 5]
     assert torch.equal(q[3:], c.q[8:10]) and torch.equal(k[4:], c.k[10:11])
+
+
+def test_peer_ptrs_offsets_follow_the_view():
+    """PeerOutputs.peer_ptrs gives, for a view into this rank's buffer, the same byte offset in
+    every other rank's buffer (the address arithmetic only; the IPC mapping needs GPUs)."""
+    import torch
+
+    from inkling_fa4.sharding import PeerOutputs, head_shard
+
+    po = object.__new__(PeerOutputs)
+    po.local = torch.empty((10, 8, 128), dtype=torch.bfloat16)
+    po.rank, po.world = 1, 4
+    po.bases = [1 << 40, po.local.data_ptr(), 3 << 40, 5 << 40]
+    sh = head_shard(8, 4, 4, 1)
+    view = po.local[:, sh.q_lo:sh.q_hi]
+    off = sh.q_lo * 128 * 2
+    assert po.peer_ptrs(view) == [(1 << 40) + off, (3 << 40) + off, (5 << 40) + off]
+    with pytest.raises(ValueError):
+        po.peer_ptrs(torch.empty(4, dtype=torch.bfloat16))
