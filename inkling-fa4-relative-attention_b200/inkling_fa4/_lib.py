@@ -127,6 +127,27 @@ class Ifa4Error(RuntimeError):
 
 
 _lib = None
+_torch_ops = None
+TORCH_OPS_PATH = os.path.join(_LIB_DIR, "libifa4_torch_ops.so")
+
+
+def torch_ops():
+    """The torch operators ``torch.ops.inkling_fa4`` over the C ABI (``prefill_``, ``decode_``),
+    or None when they are not built or the debug library is selected (they link the release
+    library).  The package then calls the C ABI through ctypes instead: the same entry points,
+    with more host work per call."""
+    global _torch_ops
+    if _torch_ops is not None:
+        return _torch_ops or None
+    _torch_ops = False
+    if os.environ.get("INKLING_FA4_LIB") == "debug" or not os.path.exists(TORCH_OPS_PATH):
+        return None
+    import torch
+
+    lib()  # load the C ABI first (one shared instance: status word, last-error message)
+    torch.ops.load_library(TORCH_OPS_PATH)
+    _torch_ops = torch.ops.inkling_fa4
+    return _torch_ops
 
 
 def lib() -> ctypes.CDLL:

@@ -12,6 +12,9 @@ from . import _lib
 
 HEAD_DIM = 128
 ALIGN = {"reference": _lib.IFA4_ALIGN_REFERENCE, "bottom_right": _lib.IFA4_ALIGN_BOTTOM_RIGHT}
+# Launch through the torch operators (csrc/ifa4_torch_ops.cpp) when they are built; False (or an
+# unbuilt operator library) keeps every launch on the ctypes calls of the same C ABI.
+USE_TORCH_OPS = True
 
 
 def _tma_ready(t: torch.Tensor) -> torch.Tensor:
@@ -184,6 +187,16 @@ def prefill(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_s
         "prefill", q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, rel_extent, causal,
         window_size, n_heads, kv_heads, head_dim, softmax_scale, causal_align, out, block_table)
     lse = _lse_buffer(q, n_heads, return_lse, lse)
+    ops = _lib.torch_ops() if USE_TORCH_OPS and not out_peers else None
+    if ops is not None:  # one dispatcher call: parameter block, stream, workspace, launch
+        rc = ops.prefill_(q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, lse, block_table,
+                          workspace, rel_extent, bool(causal), window_left, ALIGN[causal_align],
+                          int(max_seqlen_q) if max_seqlen_q else 0,
+                          int(max_seqlen_k) if max_seqlen_k else 0, scale, int(tile_config),
+                          int(kv_splits))
+        if rc:
+            _lib.check(rc)
+        return (out, lse) if lse is not None else out
     p = _lib.PrefillParams()
     _fill_lse(p, lse)
     _fill_common(p, q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
@@ -256,6 +269,15 @@ def decode(q, k, v, rel_logits, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_se
         raise ValueError("decode: expects exactly one query token per sequence")
     if q.stride(0) % 2 or q.stride(1) % 2:
         q = q.contiguous()
+    ops = _lib.torch_ops() if USE_TORCH_OPS else None
+    if ops is not None:  # one dispatcher call: parameter block, stream, workspace, launch
+        rc = ops.decode_(q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, lse, block_table,
+                         workspace, rel_extent, bool(causal), window_left, ALIGN[causal_align],
+                         int(max_seqlen_k) if max_seqlen_k else 0, scale, int(num_splits),
+                         int(chunk_len))
+        if rc:
+            _lib.check(rc)
+        return (out, lse) if lse is not None else out
     p = _decode_params(q, k, v, rel, out, cu_seqlens_q, cu_seqlens_k, n_heads, kv_heads,
                        rel_extent, causal, window_left, causal_align, max_seqlen_k, scale,
                        num_splits, chunk_len, block_table)

@@ -244,3 +244,15 @@ def test_prefill_workspace_size_of_an_empty_batch_is_zero():
     assert nbytes.value == 0
     assert L.ifa4_prefill_workspace_size(ctypes.byref(_valid_prefill()), None) == \
         _lib.IFA4_ERR_INVALID_ARGUMENT
+
+
+def test_torch_operator_library_registers_its_schemas():
+    """The operator library loads without a GPU and declares prefill_ / decode_ (the package's
+    launch path); its CUDA kernels run only in the GPU tests."""
+    import torch
+    ops = _lib.torch_ops()
+    assert ops is not None, "libifa4_torch_ops.so not built"
+    for name in ("prefill_", "decode_"):
+        schema = str(getattr(ops, name).default._schema)
+        assert schema.startswith(f"inkling_fa4::{name}(Tensor q")
+    assert torch.ops.inkling_fa4 is ops
