@@ -1071,9 +1071,10 @@ def main():
                 "host_us_per_call": host_us, "device_us_per_call_median": smed * 1e3,
                 "device_us_per_call_graph_replay": sgraph,
                 "kv_tokens": small.max_k,
-                "note": "wall clock of 200 back-to-back Python calls (argument checks, ctypes "
-                        "struct, plan query, 2 launches) vs CUDA-event device time; the host "
-                        "cost hides behind the device when it is the smaller"},
+                "note": "wall clock of 200 back-to-back Python calls (argument checks, one "
+                        "torch-operator call that fills the C ABI's parameter block, plans, "
+                        "allocates the workspace and makes 2 launches) vs CUDA-event device "
+                        "time; the host cost hides behind the device when it is the smaller"},
             "gpu_launches": steps2 * (2 if nsplit > 1 else 1)}
         del small, sws
         # the same step against a 16-token paged cache (pages handed out in random order)
