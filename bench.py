@@ -958,6 +958,8 @@ def main():
                                "every rank's [T, 32, 128] buffer (CUDA IPC peer mappings, plain "
                                "16-byte stores over NVLink) as its tiles finish; one 4-byte NCCL "
                                "all-reduce per step orders the reads"})
+        if peers is not None:
+            peers.close()  # every rank unmaps the others' buffers before any rank frees its own
         del sc, q_s, k_s, v_s, rel_s, full, ref, src, gbuf, fused, peers
         torch.cuda.empty_cache()
 

@@ -153,7 +153,10 @@ class PeerOutputs:
         off = view.data_ptr() - self.local.data_ptr()
         if not 0 <= off < self.local.numel() * self.local.element_size():
             raise ValueError("view does not start inside this rank's buffer")
-        return [b + off for r, b in enumerate(self.bases) if r != self.rank]
+        peers = [b for r, b in enumerate(self.bases) if r != self.rank]
+        if any(b is None for b in peers):
+            raise RuntimeError("PeerOutputs is closed: the other ranks' buffers are unmapped")
+        return [b + off for b in peers]
 
     def barrier(self):
         """Stream-ordered barrier over the ranks (a one-element NCCL all-reduce on the current
@@ -162,6 +165,21 @@ class PeerOutputs:
         import torch.distributed as dist
 
         dist.all_reduce(self._flag, group=self.group)
+
+    def close(self):
+        """Collective: unmap the other ranks' buffers, then wait until every rank has unmapped
+        them, so that no rank frees its buffer (or exits) while another rank still maps it.
+        ``local`` stays valid; ``peer_ptrs`` may not be used afterwards."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.local.device)  # no kernel of this rank still stores
+        dist.all_reduce(self._flag, group=self.group)  # ... nor of any other rank
+        torch.cuda.synchronize(self.local.device)
+        self._mapped.clear()
+        self.bases = [self.local.data_ptr() if r == self.rank else None
+                      for r in range(self.world)]
+        dist.all_reduce(self._flag, group=self.group)  # every rank has unmapped
+        torch.cuda.synchronize(self.local.device)
 
 
 def prefill_to_all_ranks(peers: PeerOutputs, sh: HeadShard, q, k, v, rel, cu_seqlens_q,

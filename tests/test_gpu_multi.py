@@ -53,6 +53,8 @@ def _rank_main(rank, world, port, q_out):
             fused.append(prefill_to_all_ranks(peers, sh, q, k, v, rel, c.cu_q, c.cu_k, 1000, 1000,
                                               128).clone())
             peers.barrier()
+        peers.close()  # collective: no rank frees its buffer while another still maps it
+        closed_ok = all(b is None for r, b in enumerate(peers.bases) if r != rank)
         d = make_case([1] * 4, [3000, 70, 5000, 640], 16, 4, 128, seed=78, device=dev)
         dq, dk, dv, drel = shard_tensors(sh, d.q, d.k, d.v, d.rel)
         # a fixed split plan keeps the per-head arithmetic identical to the unsharded call
@@ -68,7 +70,7 @@ def _rank_main(rank, world, port, q_out):
                                                            5000, 128, causal_align="bottom_right",
                                                            num_splits=4, chunk_len=512)
             q_out.put((bool(torch.equal(full, ref)), bool(torch.equal(dfull, dref)),
-                       all(bool(torch.equal(f, ref)) for f in fused)))
+                       all(bool(torch.equal(f, ref)) for f in fused) and closed_ok))
         dist.barrier()
     finally:
         dist.destroy_process_group()

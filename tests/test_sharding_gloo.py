@@ -120,3 +120,6 @@ def test_peer_ptrs_offsets_follow_the_view():
     assert po.peer_ptrs(view) == [(1 << 40) + off, (3 << 40) + off, (5 << 40) + off]
     with pytest.raises(ValueError):
         po.peer_ptrs(torch.empty(4, dtype=torch.bfloat16))
+    po.bases = [None, po.local.data_ptr(), None, None]  # the state close() leaves
+    with pytest.raises(RuntimeError):
+        po.peer_ptrs(view)
