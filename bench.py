@@ -501,7 +501,8 @@ def read_stream_peak(dev, stream):
     return nbytes / (best / 1e3) / 1e9
 
 
-def main():
+def parse_args(argv=None):
+    """(args, the set of legs to skip, whether the headline runs)."""
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -526,10 +527,17 @@ def main():
                     help="prefill kernel variant (0 = default; see autotune_configs)")
     ap.add_argument("--decode-batch", type=int, default=128,
                     help="decode batch (128 = BASELINE config 5)")
-    args = ap.parse_args()
+    # earlier spellings, kept so that the capture commands recorded with the profiles still run:
+    # --no-<leg> is --skip <leg>, --only prefill is --only headline
+    for leg in ("e2e", "decode", "window", "backward", "rel-logits"):
+        ap.add_argument(f"--no-{leg}", action="append_const", dest="old_skip",
+                        const=leg.replace("-", "_"), help=argparse.SUPPRESS)
+    args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
-    skip = {s for s in args.skip.split(",") if s}
+    if args.only == "prefill":
+        args.only = "headline"
+    skip = {s for s in args.skip.split(",") if s} | set(args.old_skip or ())
     bad = skip - set(LEGS)
     if bad:
         ap.error(f"unknown legs {sorted(bad)}")
@@ -539,8 +547,12 @@ def main():
         skip = set(LEGS) - {args.only}
         args.no_shard = True
         args.no_cpu_baseline = True
+    return args, skip, args.only in ("all", "headline", "e2e")
+
+
+def main():
+    args, skip, run_headline = parse_args()
     want = lambda leg: leg not in skip
-    run_headline = args.only in ("all", "headline", "e2e")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -32,3 +32,20 @@ def test_c_level_stdout_goes_to_stderr_inside_the_guard():
     assert r.returncode == 0, r.stderr
     assert r.stdout.strip().splitlines() == ['{"metric": 1}']
     assert "NCCL version banner" in r.stderr and "python inside" in r.stderr
+
+
+def test_recorded_profile_commands_parse_to_the_legs_they_ran():
+    """The capture commands kept with the ncu summaries use the earlier --no-<leg> and
+    --only prefill spellings; they still select the same legs."""
+    args, skip, headline = bench.parse_args(
+        "--steps 5 --warmup 3 --no-e2e --no-cpu-baseline --no-decode --no-window --no-backward "
+        "--no-rel-logits".split())
+    assert headline and args.no_cpu_baseline and args.steps == 5
+    assert {"e2e", "decode", "window", "backward", "rel_logits"} <= skip
+    args, skip, headline = bench.parse_args(
+        "--only prefill --prefill-seq 8192 --steps 2 --warmup 3 --no-e2e --no-window".split())
+    assert headline and args.prefill_seq == 8192 and skip == set(bench.LEGS)
+    args, skip, headline = bench.parse_args([])
+    assert headline and not skip and args.warmup == 5
+    args, skip, headline = bench.parse_args(["--only", "decode"])
+    assert not headline and skip == set(bench.LEGS) - {"decode"}
