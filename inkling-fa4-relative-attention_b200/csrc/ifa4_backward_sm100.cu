@@ -400,7 +400,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool has_bias = key_valid && dq0 + half * 64 <= a.rel_extent - 1 &&
                               dq0 + half * 64 + 63 >= 0;
         const bool warp_bias = __any_sync(0xffffffffu, has_bias);
-        const bool warp_slow = __any_sync(0xffffffffu, has_mask || has_bias);
+        const bool warp_slow = __any_sync(0xffffffffu, has_mask);  // bias: folded into nlr
+        // The bias of a band step is read one value per (key, query) pair: for each of the 64
+        // columns the warp's 32 keys read 32 consecutive distances (64 bytes) of that query's
+        // rel row, a different row per column.  Those lines are pulled into L2 one step ahead,
+        // so the step's loads wait on L2 rather than on DRAM: lane l takes columns l and l + 32,
+        // at the distances of the warp's first and last key (in bounds by construction).
+        if (n + 1 < steps) {
+          const int g1 = (n + 1) / blk.n_q;
+          const int q1 = (blk.i_lo + n + 1 - g1 * blk.n_q) * kBM;
+          const int kl0 = k0 + quarter * 32;            // the warp's first key
+          const int d_hi0 = q1 + bs - kl0 + half * 64;  // distance of (first key, column 0)
+          const int d_lo0 = d_hi0 - 31;                 // (last key, column 0)
+          if (d_lo0 <= a.rel_extent - 1 && d_hi0 + 63 >= 0) {  // some pair is in the band
+            const uint16_t* rel_h1 = a.rel + static_cast<long long>(kvh * group + g1) * a.rel_sh;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int c = lane + 32 * k;
+              const int qq = q1 + half * 64 + c;
+              const int lo = max(d_lo0 + c, 0), hi = min(d_hi0 + c, a.rel_extent - 1);
+              if (qq < sq && lo <= hi) {
+                const uint16_t* row = rel_h1 + static_cast<long long>(q_start + qq) * a.rel_st;
+                prefetch_l2(row + lo);
+                prefetch_l2(row + hi);
+              }
+            }
+          }
+        }
         // -lse2 of the 64 columns into registers while S^T is computed: during the P phase the
         // tensor core streams dK / dP^T operands out of shared memory, and column loads issued
         // then stall the exponentials behind them
@@ -413,6 +439,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           nlr[c + 2] = L.z;
           nlr[c + 3] = L.w;
         }
+        // Band step: the bias joins the exponent's per-column term, log2(e) * rel - lse2, here,
+        // before the wait for S^T, so the loads' round trips overlap the S^T product rather than
+        // the P phase (16 loads in flight at a time).
+        if (warp_bias) {
+          const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
+#pragma unroll
+          for (int c16 = 0; c16 < 64; c16 += 16) {
+            float b[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int cq = half * 64 + c16 + i;
+              const int d = dq0 + cq;
+              b[i] = 0.f;
+              if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
+                b[i] = bf16_bits_to_float(
+                    __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) nlr[c16 + i] = fmaf(b[i], kLog2e, nlr[c16 + i]);
+          }
+        }
         if (!(ok = mbar_wait_warp(&bars->s_full, sc & 1, ab))) break;
         tc_fence_after();
         {
@@ -423,36 +470,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t sr[32];
             tmem_ld32(t_s + c2 * 32, sr);
             tmem_wait_ld();
-            if (!warp_slow) {  // interior tile: p = 2^(s * scale * log2e - lse2)
+            if (!warp_slow) {  // unmasked tile: p = 2^(s * scale * log2e + log2e * rel - lse2)
 #pragma unroll
               for (int i = 0; i < 32; i += 2) {
                 const float x0 = fmaf(__uint_as_float(sr[i]), a.scale_log2, nlr[c2 * 32 + i]);
                 const float x1 = fmaf(__uint_as_float(sr[i + 1]), a.scale_log2, nlr[c2 * 32 + i + 1]);
                 pk[c2 * 16 + i / 2] = pack_bf16x2(fast_exp2(x0), fast_exp2(x1));
               }
-            } else {
-              const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
+            } else {  // masked tile (any bias is already in nlr): p = 0 where masked
 #pragma unroll
-              for (int i16 = 0; i16 < 32; i16 += 16) {  // 16 bias loads in flight at a time
-                float p[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  const int c = c2 * 32 + i16 + i;
-                  const int cq = half * 64 + c;
-                  float bias = 0.f;
-                  if (warp_bias) {
-                    const int d = dq0 + cq;
-                    if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0)
-                      bias = bf16_bits_to_float(
-                          __ldg(rel_h + static_cast<long long>(q_start + q0 + cq) * a.rel_st + d));
-                  }
-                  p[i] = fast_exp2(fmaf(__uint_as_float(sr[i16 + i]), a.scale_log2,
-                                        fmaf(bias, kLog2e, nlr[c])));
-                  if (has_mask && (cq < c_lo || cq >= c_hi)) p[i] = 0.f;
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) pk[c2 * 16 + i16 / 2 + i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
-                __syncwarp();
+              for (int i = 0; i < 32; i += 2) {
+                const int c = c2 * 32 + i;
+                const int cq = half * 64 + c;
+                float p0 = fast_exp2(fmaf(__uint_as_float(sr[i]), a.scale_log2, nlr[c]));
+                float p1 = fast_exp2(fmaf(__uint_as_float(sr[i + 1]), a.scale_log2, nlr[c + 1]));
+                if (has_mask && (cq < c_lo || cq >= c_hi)) p0 = 0.f;
+                if (has_mask && (cq + 1 < c_lo || cq + 1 >= c_hi)) p1 = 0.f;
+                pk[c2 * 16 + i / 2] = pack_bf16x2(p0, p1);
               }
             }
           }
