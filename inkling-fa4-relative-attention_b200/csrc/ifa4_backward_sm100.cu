@@ -129,7 +129,13 @@ constexpr uint32_t kSmemDO = 4 * kTile;  // 2 stages
 constexpr uint32_t kSmemBar = 6 * kTile;
 // per elementwise warp, two buffers of -lse (log2 domain) and Delta of its 64 query columns
 constexpr uint32_t kSmemVec = kSmemBar + 256;
-constexpr uint32_t kSmemBytes = kSmemVec + 8 * 256 * 4;
+// per elementwise warp, the relative-bias segments of 32 of its columns in a band step: five
+// aligned 16-byte vectors (80 bytes) around the 32 distances its keys read in each column
+constexpr uint32_t kStageColBytes = 80;
+constexpr uint32_t kStageWarpBytes = 32 * kStageColBytes;
+constexpr uint32_t kSmemStage = kSmemVec + 8 * 256 * 4;
+constexpr uint32_t kSmemBytes = kSmemStage + 8 * kStageWarpBytes;
+static_assert(kSmemBytes + 1024 <= 227u * 1024u, "dK/dV shared memory");
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
 
@@ -442,7 +448,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Band step: the bias joins the exponent's per-column term, log2(e) * rel - lse2, here,
         // before the wait for S^T, so the loads' round trips overlap the S^T product rather than
         // the P phase (16 loads in flight at a time).
-        if (warp_bias) {
+        if (warp_bias && a.bias_vec) {
+          // The warp's 32 keys read, in column c, the 32 distances [dh + c - 31, dh + c] of that
+          // query's rel row.  Per half of the columns the 32 segments go to shared memory as
+          // five aligned 16-byte vectors each (cp.async: no registers held while in flight;
+          // vectors outside [0, R) or past the sequence are not copied and not read), then each
+          // lane reads its own 32 values: one round trip per half.
+          const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
+          const int dh = q0 + bs - (k0 + quarter * 32) + half * 64;
+          const uint8_t* stg = smem + kv::kSmemStage + (warp - 2) * kv::kStageWarpBytes;
+          const uint32_t stg_s = smem_u32(stg);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int m = 0; m < 5; ++m) {
+              const int t = lane + 32 * m;  // vector t of 160: column j, vector v
+              const int j = t / 5, v = t - 5 * j;
+              const int qq = q0 + half * 64 + hh * 32 + j;
+              const int st = ((dh + hh * 32 + j - 31) & ~7) + 8 * v;
+              if (qq < sq && st >= 0 && st < a.rel_extent)
+                cp_async16(stg_s + j * kv::kStageColBytes + v * 16,
+                           rel_h + static_cast<long long>(q_start + qq) * a.rel_st + st);
+            }
+            cp_async_wait_all();
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int c = hh * 32 + i;
+              const int cq = half * 64 + c;
+              const int d = dq0 + cq;  // = dh + c - (this lane's key offset in the warp)
+              float b = 0.f;
+              if (has_bias && d >= 0 && d < a.rel_extent && cq < sq - q0) {
+                const int base = (dh + c - 31) & ~7;
+                b = bf16_bits_to_float(*reinterpret_cast<const uint16_t*>(
+                    stg + i * kv::kStageColBytes + (d - base) * 2));
+              }
+              nlr[c] = fmaf(b, kLog2e, nlr[c]);
+            }
+            __syncwarp();  // every lane has read the stage before the next half overwrites it
+          }
+        } else if (warp_bias) {  // unaligned or odd-extent bias tensor: one load per value
           const uint16_t* rel_h = a.rel + static_cast<long long>(h) * a.rel_sh;
 #pragma unroll
           for (int c16 = 0; c16 < 64; c16 += 16) {
