@@ -68,7 +68,7 @@ NCU_DRAM_BYTES_PER_LAUNCH = {
 }
 
 LEGS = ("e2e", "window", "ragged", "chunked", "global_rel1024", "local_rel512",
-        "refbench", "config1", "backward", "rel_logits", "decode")
+        "refbench", "config1", "backward", "backward_rel1024", "rel_logits", "decode")
 
 
 def load_peaks():
@@ -753,31 +753,30 @@ def main():
                                           {"workload": "window4096_32k_gqa32_8_d128_rel128",
                                            "window_left": 4096}, window_size=(4096, 0))
 
-    # ---------------- backward of the headline prefill (not in the reference)
-    if want("backward"):
+    # ---------------- backward of a prefill (not in the reference)
+    def backward_leg(bc, rext, bflops):
         from inkling_fa4 import inkling_fa4_rel_attention_backward
 
-        bout, blse = inkling_fa4_rel_attention_triton(c.q, c.k, c.v, c.rel, c.cu_q, c.cu_k, S, S,
-                                                      R, return_lse=True)
+        bout, blse = inkling_fa4_rel_attention_triton(bc.q, bc.k, bc.v, bc.rel, bc.cu_q, bc.cu_k,
+                                                      S, S, rext, return_lse=True)
         gen = torch.Generator(device=dev)
         gen.manual_seed(1000 + rank)
-        bdout = torch.randn(c.q.shape, generator=gen, device=dev).to(torch.bfloat16)
+        bdout = torch.randn(bc.q.shape, generator=gen, device=dev).to(torch.bfloat16)
         bws = torch.empty(HQ * S * 4, dtype=torch.uint8, device=dev)
-        bufs = (torch.empty_like(c.q), torch.empty_like(c.k), torch.empty_like(c.v),
-                torch.empty_like(c.rel))
+        bufs = (torch.empty_like(bc.q), torch.empty_like(bc.k), torch.empty_like(bc.v),
+                torch.empty_like(bc.rel))
 
         def bwd_step():
             return inkling_fa4_rel_attention_backward(
-                bdout, c.q, c.k, c.v, c.rel, bout, blse, c.cu_q, c.cu_k, S, S, R, dq=bufs[0],
-                dk=bufs[1], dv=bufs[2], drel=bufs[3], workspace=bws)
+                bdout, bc.q, bc.k, bc.v, bc.rel, bout, blse, bc.cu_q, bc.cu_k, S, S, rext,
+                dq=bufs[0], dk=bufs[1], dv=bufs[2], drel=bufs[3], workspace=bws)
 
         bsteps = max(5, args.steps // 2)
         bms, bmed = timed(bwd_step, bsteps, args.warmup, stream, dist, barrier)
-        bflops = 2.5 * flops  # 5 matrix products of the forward's size (the usual convention)
-        result["backward32k"] = {
+        leg = {
             "value": world * bflops * bsteps / (bms / 1e3) / 1e12, "unit": "TFLOP/s",
             "ms_per_step": bms / bsteps, "ms_per_step_median": bmed, "steps": bsteps,
-            "flops_per_step_per_gpu": bflops,
+            "rel_extent": rext, "flops_per_step_per_gpu": bflops,
             "flops_note": "algorithmic 2.5x forward (S, dP, dV, dK, dQ); the kernels execute "
                           "3.5x (S and dP are recomputed by the dQ kernel to avoid atomics)",
             "roofline": dict(tensor_roofline(bflops, bmed), kernel="rel_attn_bwd_prep_kernel, "
@@ -785,6 +784,10 @@ def main():
                              "step; algorithmic FLOPs over the whole step)"),
             "gpu_launches": 3 * bsteps}
         del bout, blse, bdout, bws, bufs
+        return leg
+
+    if want("backward"):  # of the headline prefill
+        result["backward32k"] = backward_leg(c, R, 2.5 * flops)
 
     # ---------------- rel_logits producer for the headline shape (the step before the path)
     if want("rel_logits"):
@@ -855,10 +858,12 @@ def main():
     # Global layers: R = 1024, full causal; local layers: R = 512 with window (511, 0)
     # (the reference's architecture notes); the reference's benchmark: S = 4096, Hq = Hkv = 4,
     # R = 1024, causal (its only published numbers).
+    # The global layers' backward (same inputs as the R = 1024 forward leg) as backward_rel1024.
     for name, seq, hq, hkv, rext, win in (("global_rel1024", S, HQ, HKV, 1024, None),
                                           ("local_rel512", S, HQ, HKV, 512, 511),
                                           ("refbench", 4096, 4, 4, 1024, None)):
-        if not want(name):
+        with_bwd = name == "global_rel1024" and want("backward_rel1024")
+        if not want(name) and not with_bwd:
             continue
         gc = make_case([seq], [seq], hq, hkv, rext, seed=rank, device=dev, rel_std=0.5,
                        gen_device=dev)
@@ -866,13 +871,16 @@ def main():
         kw = {} if win is None else {"window_size": (win, 0)}
         key = {"global_rel1024": f"global{seq}_rel1024", "local_rel512": f"local{seq}_rel512_window511",
                "refbench": "refbench4096_h4_rel1024"}[name]
-        leg = prefill_leg(key, gc, fl, steps2, warm2,
-                          {"workload": f"{key}_gqa{hq}_{hkv}_d128", "seq_len": seq,
-                           "window_left": win}, **kw)
-        if name == "refbench":
-            leg["reference_published_ms_rtx3090"] = REF_PUBLISHED_MS_S4096
-            leg["speedup_vs_published"] = REF_PUBLISHED_MS_S4096 / leg["ms_per_step_median"]
-        result[key] = leg
+        if want(name):
+            leg = prefill_leg(key, gc, fl, steps2, warm2,
+                              {"workload": f"{key}_gqa{hq}_{hkv}_d128", "seq_len": seq,
+                               "window_left": win}, **kw)
+            if name == "refbench":
+                leg["reference_published_ms_rtx3090"] = REF_PUBLISHED_MS_S4096
+                leg["speedup_vs_published"] = REF_PUBLISHED_MS_S4096 / leg["ms_per_step_median"]
+            result[key] = leg
+        if with_bwd:
+            result[f"backward{seq}_rel1024"] = backward_leg(gc, rext, 2.5 * fl)
         del gc
         torch.cuda.empty_cache()
 
