@@ -466,7 +466,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int j = t / 5, v = t - 5 * j;
               const int qq = q0 + half * 64 + hh * 32 + j;
               const int st = ((dh + hh * 32 + j - 31) & ~7) + 8 * v;
-              if (qq < sq && st >= 0 && st < a.rel_extent)
+              if (qq < sq && st >= 0 && st < a.rel_extent &&
+                  IFA4_DBG_CHECK(a.status, q_start + qq < a.total_q))
                 cp_async16(stg_s + j * kv::kStageColBytes + v * 16,
                            rel_h + static_cast<long long>(q_start + qq) * a.rel_st + st);
             }
