@@ -2,7 +2,8 @@
 //
 // One CTA owns two 128-row query sub-tiles that share a KV head ("ping-pong"): either two
 // query heads of one GQA group at the same rows (even group size), or two consecutive 128-row
-// blocks of one head.  Warp roles (12 warps, 384 threads):
+// blocks of one head.  Warp roles (12 warps, 384 threads; after set-up setmaxnreg leaves warps
+// 0-3 56 registers each and gives the softmax warps 224):
 //   warp 0      TMA producer: Q sub-tiles once per work tile, then K/V tiles through a
 //               two-stage ring (128 keys x 128 dims, 128-byte swizzle, no multicast).
 //   warp 1      UMMA issuer (one thread): S_s = Q_s K^T (SS, both K-major) into TMEM, then
@@ -48,6 +49,10 @@ namespace prefill {
 constexpr int kBM = 128;                                 // query rows per sub-tile
 constexpr int kBN = 128;                                 // keys per KV tile
 constexpr int kThreads = 384;
+// register split after set-up: warps 0-3 (producer, MMA issuer, TMEM owner) give registers to the
+// eight softmax warps, 4 x 32 x 56 + 8 x 32 x 224 = 64512 = 384 threads x 168 at launch
+constexpr int kRegsControl = 56, kRegsSoftmax = 224;
+static_assert(4 * 32 * kRegsControl + 8 * 32 * kRegsSoftmax <= 384 * 168, "register split");
 constexpr uint32_t kHalf = 128u * 128u;                  // 128 rows x 128 B (64 dims)
 constexpr uint32_t kTile = 2u * kHalf;                   // 128 rows x 256 B (128 dims)
 constexpr uint32_t kSmemQ = 0;                           // 2 sub-tiles
@@ -332,6 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
   const AbortCtx ab{&bars->abort_flag, a.status, kStatusPrefillTimeout};
+  if (warp < 4) setmaxnreg_dec<kRegsControl>();
+  else setmaxnreg_inc<kRegsSoftmax>();
   if (warp < 4) {
    if (kPaged && warp == 0) {
     produce_paged<kSplit>(a, smem, bars, &tm_q, &tm_k, &tm_v, hslot, b, q_start, sq, sk, n_qt,

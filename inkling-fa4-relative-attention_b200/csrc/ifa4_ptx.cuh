@@ -505,11 +505,12 @@ __device__ __forceinline__ void load_bias_window(const uint16_t* rel_row, int dt
   }
 }
 
-// x[i] += log2(e) * bias of column i of chunk cc, from the window above: column i has distance
+// b[i] = bias of column i of chunk cc, from the window above: column i has distance
 // dtop - 32 cc - i = element (off + 31 - i) of the window, off = (dtop - 32 cc - 31) mod 8; the
 // window is shifted by off elements with selects and a byte permute (no shared memory).
-__device__ __forceinline__ void add_bias_window(const uint32_t (&w)[20], int dtop, int cc,
-                                                float (&x)[32]) {
+// Columns outside [0, rel_extent) read 0 from the zero-filled vectors.
+__device__ __forceinline__ void bias_window_floats(const uint32_t (&w)[20], int dtop, int cc,
+                                                   float (&b)[32]) {
   const int off = (dtop - 32 * cc - 31) & 7;
   const int q = off >> 1;  // whole words to skip
   uint32_t t2[17];
@@ -521,8 +522,28 @@ __device__ __forceinline__ void add_bias_window(const uint32_t (&w)[20], int dto
   for (int i = 0; i < 32; ++i) {
     const int j = 31 - i;  // element j of the shifted window
     const uint32_t pr = __byte_perm(t2[j >> 1], t2[(j >> 1) + 1], sel);
-    x[i] += __uint_as_float((j & 1) ? (pr & 0xffff0000u) : (pr << 16)) * 1.4426950408889634f;
+    b[i] = __uint_as_float((j & 1) ? (pr & 0xffff0000u) : (pr << 16));
   }
+}
+
+// x[i] += log2(e) * bias of column i of chunk cc.
+__device__ __forceinline__ void add_bias_window(const uint32_t (&w)[20], int dtop, int cc,
+                                                float (&x)[32]) {
+  float b[32];
+  bias_window_floats(w, dtop, cc, b);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] += b[i] * 1.4426950408889634f;
+}
+
+// Warpgroup-wide register re-split (every warp of the warpgroup executes it; the sum over the
+// CTA's warps must fit in the registers the CTA was launched with).
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegs) : "memory");
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegs) : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
